@@ -1,0 +1,966 @@
+// C ABI of the B200 fused causal softmax: argument checks, kernel selection,
+// launch geometry, plans, one-shot launches and host-buffer sessions.
+//
+// This file replaces the reference's typed dispatch boundary
+// (gpu/src/driver.rs:12-233) and its TMA descriptor setup
+// (gpu/src/main.rs:730-774). Kernels come from kernels/*.cuh.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "causal_softmax.h"
+#include "kernels/baseline.cuh"
+#include "kernels/narrow.cuh"
+#include "kernels/online.cuh"
+#include "kernels/rowres.cuh"
+#include "kernels/util.cuh"
+
+namespace {
+
+using cs::Geometry;
+
+constexpr int kMaxDevices = 64;
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s of GPU time per wait
+constexpr int kDefaultStages = 3;
+constexpr int kOnlineDefaultStages = 8;
+constexpr int64_t kI32Max = 2147483647;
+constexpr int64_t kMaxUnitsPerLaunch = int64_t(1) << 30;  // row-resident kernel, 32-bit unit index
+
+thread_local char t_detail[256];
+
+int cuda_fail(cudaError_t e, const char* what) {
+  std::snprintf(t_detail, sizeof t_detail, "%s: %s", what, cudaGetErrorString(e));
+  return CS_ERR_CUDA;
+}
+
+#define CS_CUDA(call)                                 \
+  do {                                                \
+    cudaError_t _e = (call);                          \
+    if (_e != cudaSuccess) return cuda_fail(_e, #call); \
+  } while (0)
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int major = 0, minor = 0;
+  int max_smem_optin = 0;
+  uint32_t* oneshot_status = nullptr;  // status word for cs_softmax*
+  bool attrs_set = false;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    if (prev_ != dev) ok_ = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev_ >= 0 && ok_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = -1;
+  bool ok_ = true;
+};
+
+template <int V, int MAXT, bool TS>
+void* rowres_fn() {
+  return reinterpret_cast<void*>(&cs::rowres_kernel<V, MAXT, TS>);
+}
+
+// Maximum CTA size per vectors-per-thread choice (V) of the row-resident
+// kernel, which fixes its register budget: V = 2 runs with up to 1024
+// threads (64 registers), V = 4 with up to 768 (85), V = 8 with up to 576 (113).
+constexpr int rowres_maxt(int v) { return v == 8 ? 576 : (v == 4 ? 768 : 1024); }
+
+void* rowres_kernel_ptr(int v, bool tma_store) {
+  if (tma_store) {
+    switch (v) {
+      case 2: return rowres_fn<2, 1024, true>();
+      case 4: return rowres_fn<4, 768, true>();
+      default: return rowres_fn<8, 576, true>();
+    }
+  }
+  switch (v) {
+    case 2: return rowres_fn<2, 1024, false>();
+    case 4: return rowres_fn<4, 768, false>();
+    default: return rowres_fn<8, 576, false>();
+  }
+}
+
+// Per-device properties and one-time kernel attributes (max dynamic smem).
+int device_info(int dev, DeviceInfo** out) {
+  if (dev < 0 || dev >= kMaxDevices) return CS_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || dev >= n) {
+      std::snprintf(t_detail, sizeof t_detail, "device %d not present (%d devices)", dev, n);
+      return CS_ERR_DEVICE;
+    }
+    CS_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    CS_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+    CS_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+    CS_CUDA(cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (d.major != 10) {
+      std::snprintf(t_detail, sizeof t_detail, "sm_100a build needs compute capability 10.x, found %d.%d",
+                    d.major, d.minor);
+      return CS_ERR_DEVICE;
+    }
+    d.ready = true;
+  }
+  if (!d.attrs_set) {
+    DeviceGuard guard(dev);
+    if (!guard.ok()) return CS_ERR_DEVICE;
+    for (int ts = 0; ts < 2; ++ts)
+      for (int v : {2, 4, 8})
+        CS_CUDA(cudaFuncSetAttribute(rowres_kernel_ptr(v, ts != 0),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return CS_OK;
+}
+
+int64_t padded_pitch(int64_t cols) { return (cols + 7) & ~int64_t(7); }
+
+bool is_known_kernel(int k) { return k >= CS_KERNEL_AUTO && k <= CS_KERNEL_ONLINE; }
+
+// Causal element count of rows [row_offset, row_offset + rows).
+double causal_elements(int64_t rows, int64_t cols, int64_t row_offset) {
+  int64_t tri = cols - 1 - row_offset;
+  if (tri < 0) tri = 0;
+  if (tri > rows) tri = rows;
+  const double t = (double)tri;
+  return t * (double)(row_offset + 1) + t * (t - 1.0) / 2.0 + (double)(rows - tri) * (double)cols;
+}
+
+int validate_args(int64_t batch, int64_t batch_stride, int64_t rows, int64_t cols, int64_t pitch,
+                  int64_t row_offset, float scale) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return CS_ERR_EMPTY;
+  if (rows > kI32Max || cols > kI32Max || row_offset < 0 || row_offset > kI32Max - rows)
+    return CS_ERR_WRONG_LENGTH;
+  if (pitch < cols || (pitch & 7) != 0 || pitch > kI32Max) return CS_ERR_PITCH;
+  if (!std::isfinite(scale) || !(scale >= 0.0f && scale <= CS_MAX_SCALE)) return CS_ERR_BAD_SCALE;
+  const int64_t mat = rows * pitch;  // < 2^62
+  if (batch > 1) {
+    if (batch_stride < mat || (batch_stride & 7) != 0) return CS_ERR_WRONG_LENGTH;
+    if (batch - 1 > (INT64_MAX - mat) / batch_stride) return CS_ERR_WRONG_LENGTH;
+  }
+  return CS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launch planning
+// ---------------------------------------------------------------------------
+
+struct Tuning {
+  int vec = 0;     // 0: automatic
+  int stages = 0;  // 0: automatic
+  int hint = -1;   // -1: automatic
+};
+
+struct LaunchPlan {
+  int kernel = 0;
+  int grid = 0, block = 0, smem = 0, stages = 0, vec = 0, ctas_per_sm = 0;
+  int64_t units = 0;
+  int narrow_lanes = 0;
+  cs::RowResParams rr{};
+  cs::OnlineParams on{};
+  cs::NarrowParams nr{};
+  cs::BaselineParams bl{};
+};
+
+int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
+  int64_t mx = 0;
+  if (m.n_pairs > 0) mx = std::max(mx, (2 * (int64_t)g.row_offset + m.n_tri + 1 + 7) / 8 + 1);
+  if (m.n_tri & 1) mx = std::max(mx, ((int64_t)g.row_offset + m.n_pairs + 1 + 7) / 8);
+  if (g.rows > m.n_tri) mx = std::max(mx, ((int64_t)g.cols + 7) / 8);
+  return mx;
+}
+
+// Row-resident kernel geometry; CS_ERR_UNSUPPORTED when a unit does not fit.
+int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tma_store,
+                LaunchPlan* lp) {
+  const cs::UnitMap m = cs::make_unit_map(g);
+  const int64_t max_nv = rowres_max_vectors(g, m);
+  int vec = 0, block = 0;
+  const int choices[3] = {2, 4, 8};
+  for (int v : choices) {
+    if (t.vec && v != t.vec) continue;
+    const int64_t thr = ((max_nv + v - 1) / v + 31) / 32 * 32;
+    if (thr <= rowres_maxt(v)) {
+      vec = v;
+      block = (int)std::max<int64_t>(thr, 32);
+      break;
+    }
+  }
+  if (!vec) {
+    std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: %lld vectors per unit do not fit",
+                  (long long)max_nv);
+    return CS_ERR_UNSUPPORTED;
+  }
+  const int stage_bytes = (int)((max_nv * 16 + 127) / 128 * 128);
+  int stages = t.stages ? t.stages : kDefaultStages;
+  while (stages > 1 && (int64_t)stages * stage_bytes + cs::rowres_tail_bytes(stages) > d.max_smem_optin)
+    --stages;
+  const int smem = stages * stage_bytes + cs::rowres_tail_bytes(stages);
+  // The bulk-store variant refills a stage one unit late, so it needs two.
+  if (smem > d.max_smem_optin || ((!t.stages || tma_store) && stages < 2)) {
+    std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: stage of %d bytes too large", stage_bytes);
+    return CS_ERR_UNSUPPORTED;
+  }
+  int per_sm = 0;
+  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(vec, tma_store),
+                                                        block, smem));
+  if (per_sm < 1) {
+    std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: no resident CTA (block %d, smem %d)",
+                  block, smem);
+    return CS_ERR_UNSUPPORTED;
+  }
+  lp->kernel = tma_store ? CS_KERNEL_PIPELINE : CS_KERNEL_TMA;
+  lp->units = m.total_units;
+  lp->grid = (int)std::min<int64_t>(m.total_units, (int64_t)d.sms * per_sm);
+  lp->block = block;
+  lp->smem = smem;
+  lp->stages = stages;
+  lp->vec = vec;
+  lp->ctas_per_sm = per_sm;
+  lp->rr.g = g;
+  lp->rr.m = m;
+  lp->rr.stages = stages;
+  lp->rr.stage_bytes = stage_bytes;
+  lp->rr.l2_hint = t.hint < 0 ? 1 : t.hint;
+  return CS_OK;
+}
+
+int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+  int stages = t.stages ? t.stages : kOnlineDefaultStages;
+  stages = std::max(1, std::min(stages, 24));
+  while (stages > 1 && (int64_t)stages * cs::kOnlineTileBytes + cs::online_tail_bytes(stages) > d.max_smem_optin)
+    --stages;
+  const int smem = stages * cs::kOnlineTileBytes + cs::online_tail_bytes(stages);
+  int per_sm = 0;
+  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &per_sm, reinterpret_cast<void*>(&cs::online_kernel), cs::kOnlineThreads, smem));
+  if (per_sm < 1) return CS_ERR_UNSUPPORTED;
+  const int64_t total_rows = g.batch * g.rows;
+  lp->kernel = CS_KERNEL_ONLINE;
+  lp->units = total_rows;
+  lp->grid = (int)std::min<int64_t>(total_rows, (int64_t)d.sms * per_sm);
+  lp->block = cs::kOnlineThreads;
+  lp->smem = smem;
+  lp->stages = stages;
+  lp->ctas_per_sm = per_sm;
+  lp->on.g = g;
+  lp->on.total_rows = total_rows;
+  lp->on.stages = stages;
+  return CS_OK;
+}
+
+int plan_narrow(const DeviceInfo& d, const Geometry& g, LaunchPlan* lp) {
+  const int nvec = (g.cols + 7) / 8;
+  if (nvec > 32) return CS_ERR_UNSUPPORTED;
+  int lanes = 1;
+  while (lanes < nvec) lanes <<= 1;
+  const int64_t total_rows = g.batch * g.rows;
+  const int64_t rows_per_block = 8 * (32 / lanes);
+  lp->kernel = CS_KERNEL_WARP;
+  lp->units = total_rows;
+  lp->block = 256;
+  lp->grid = (int)std::min<int64_t>((total_rows + rows_per_block - 1) / rows_per_block, (int64_t)d.sms * 8);
+  lp->ctas_per_sm = 8;
+  lp->narrow_lanes = lanes;
+  lp->nr.g = g;
+  lp->nr.total_rows = total_rows;
+  return CS_OK;
+}
+
+int plan_baseline(const DeviceInfo& d, const Geometry& g, LaunchPlan* lp) {
+  const int64_t total_rows = g.batch * g.rows;
+  lp->kernel = CS_KERNEL_BASELINE;
+  lp->units = total_rows;
+  lp->block = 256;
+  lp->grid = (int)std::min<int64_t>(total_rows, (int64_t)d.sms * 8);
+  lp->ctas_per_sm = 8;
+  lp->bl.g = g;
+  lp->bl.total_rows = total_rows;
+  return CS_OK;
+}
+
+// Resolve AUTO for a concrete geometry and build the launch plan.
+int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+  if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
+  switch (kernel) {
+    case CS_KERNEL_BASELINE: return plan_baseline(d, g, lp);
+    case CS_KERNEL_WARP:
+      if (g.cols > 32) {
+        std::snprintf(t_detail, sizeof t_detail, "warp specialization requires cols<=32");
+        return CS_ERR_WARP_COLS;
+      }
+      return plan_narrow(d, g, lp);
+    case CS_KERNEL_TMA: return plan_rowres(d, g, t, false, lp);
+    case CS_KERNEL_PIPELINE: return plan_rowres(d, g, t, true, lp);
+    case CS_KERNEL_ONLINE: return plan_online(d, g, t, lp);
+    default: break;
+  }
+  if (g.cols <= 32) return plan_narrow(d, g, lp);
+  const int rc = plan_rowres(d, g, t, false, lp);
+  if (rc != CS_ERR_UNSUPPORTED) return rc;
+  return plan_online(d, g, t, lp);
+}
+
+int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
+  switch (lp.kernel) {
+    case CS_KERNEL_TMA:
+    case CS_KERNEL_PIPELINE: {
+      const bool ts = lp.kernel == CS_KERNEL_PIPELINE;
+      if (lp.vec == 2) {
+        if (ts) cs::rowres_kernel<2, 1024, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<2, 1024, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+      } else if (lp.vec == 4) {
+        if (ts) cs::rowres_kernel<4, 768, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<4, 768, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+      } else {
+        if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+      }
+      break;
+    }
+    case CS_KERNEL_ONLINE:
+      cs::online_kernel<<<lp.grid, lp.block, lp.smem, stream>>>(lp.on);
+      break;
+    case CS_KERNEL_WARP:
+      switch (lp.narrow_lanes) {
+        case 1: cs::narrow_kernel<1><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        case 2: cs::narrow_kernel<2><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        case 4: cs::narrow_kernel<4><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        case 8: cs::narrow_kernel<8><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        case 16: cs::narrow_kernel<16><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        default: cs::narrow_kernel<32><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+      }
+      break;
+    case CS_KERNEL_BASELINE:
+      cs::baseline_kernel<<<lp.grid, lp.block, 0, stream>>>(lp.bl);
+      break;
+    default:
+      return CS_ERR_BAD_KERNEL;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return CS_OK;
+}
+
+double modelled_bytes(int kernel, const Geometry& g, int online_stages) {
+  const double t = causal_elements(g.rows, g.cols, g.row_offset);
+  const double w = 2.0 * (double)g.rows * (double)g.cols;
+  double per = 0;
+  switch (kernel) {
+    case CS_KERNEL_BASELINE: per = 6.0 * t + w; break;
+    case CS_KERNEL_ONLINE: {
+      // Rows longer than half the ring are fetched twice.
+      const int64_t resident_cols = (int64_t)(online_stages / 2) * cs::kOnlineTileVec * 8;
+      const double t_long = g.cols > resident_cols
+                                ? std::max(0.0, t - causal_elements(g.rows, std::min<int64_t>(g.cols, resident_cols), g.row_offset))
+                                : 0.0;
+      per = 2.0 * t + 2.0 * t_long + w;
+      break;
+    }
+    default: per = 2.0 * t + w; break;
+  }
+  return per * (double)g.batch;
+}
+
+// Launch through a geometry (plans, one-shot calls and sessions share this).
+int launch_geometry(int dev, int kernel, const Geometry& g, const Tuning& t, cudaStream_t stream,
+                    LaunchPlan* out_plan) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(dev, &d);
+  if (rc) return rc;
+  LaunchPlan lp;
+  rc = make_plan(*d, kernel, g, t, &lp);
+  if (rc) return rc;
+  if (out_plan) *out_plan = lp;
+  const bool rowres = lp.kernel == CS_KERNEL_TMA || lp.kernel == CS_KERNEL_PIPELINE;
+  if (!rowres || lp.rr.m.total_units < kMaxUnitsPerLaunch) return launch_plan(lp, stream);
+  // The row-resident kernel indexes units in 32 bits: split the batch.
+  const int64_t per = std::max<int64_t>(1, kMaxUnitsPerLaunch / lp.rr.m.units_per_matrix);
+  for (int64_t b0 = 0; b0 < g.batch; b0 += per) {
+    Geometry gc = g;
+    gc.in = g.in + b0 * g.batch_stride;
+    gc.out = g.out + b0 * g.batch_stride;
+    gc.batch = std::min<int64_t>(per, g.batch - b0);
+    LaunchPlan lc;
+    rc = make_plan(*d, lp.kernel, gc, t, &lc);
+    if (!rc) rc = launch_plan(lc, stream);
+    if (rc) return rc;
+  }
+  return CS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_pointers(const void* in, const void* out) {
+  if (!in || !out) return CS_ERR_NULL;
+  if (!aligned16(in) || !aligned16(out)) return CS_ERR_ALIGNMENT;
+  if (in == out) {
+    std::snprintf(t_detail, sizeof t_detail, "in-place softmax is not supported");
+    return CS_ERR_ARG;
+  }
+  return CS_OK;
+}
+
+int status_word_for(int dev, uint32_t** out) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(dev, &d);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!d->oneshot_status) {
+    DeviceGuard guard(dev);
+    uint32_t* p = nullptr;
+    CS_CUDA(cudaMalloc(&p, 256));
+    CS_CUDA(cudaMemset(p, 0, 256));
+    d->oneshot_status = p;
+  }
+  *out = d->oneshot_status;
+  return CS_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// Plans
+// ===========================================================================
+
+struct cs_plan {
+  int device = 0;
+  Geometry g{};
+  uint32_t* d_status = nullptr;
+  Tuning tuning{};
+};
+
+struct cs_session {
+  int device = 0;
+  cudaStream_t streams[2] = {nullptr, nullptr};
+  uint32_t* d_status = nullptr;
+  unsigned long long* d_counter = nullptr;
+  // host-path chunk buffers
+  uint16_t* d_in[2] = {nullptr, nullptr};
+  uint16_t* d_out[2] = {nullptr, nullptr};
+  size_t slot_bytes = 0;
+  // prepare / launch / result state
+  uint16_t* p_in = nullptr;
+  uint16_t* p_out = nullptr;
+  size_t p_bytes = 0;
+  int32_t p_rows = 0, p_cols = 0, p_pitch = 0;
+  bool prepared = false;
+};
+
+extern "C" {
+
+int cs_abi_version(void) { return CS_ABI_VERSION; }
+
+const char* cs_strerror(int code) {
+  switch (code) {
+    case CS_OK: return "ok";
+    case CS_ERR_EMPTY: return "matrix dimensions must be positive";
+    case CS_ERR_WRONG_LENGTH: return "score buffer length does not match matrix dimensions";
+    case CS_ERR_BAD_SCALE: return "attention scale must be finite and in [0, 1e30]";
+    case CS_ERR_NON_FINITE: return "score matrix contains NaN or infinity";
+    case CS_ERR_WARP_COLS: return "warp specialization requires cols<=32";
+    case CS_ERR_ALIGNMENT: return "base address must be nonnull and 16-byte aligned";
+    case CS_ERR_PITCH: return "pitch must be >= cols, a multiple of 8 elements and fit i32";
+    case CS_ERR_BAD_KERNEL: return "unknown kernel";
+    case CS_ERR_DEVICE: return "no usable sm_100 (compute capability 10.x) device";
+    case CS_ERR_CUDA: return "CUDA runtime error";
+    case CS_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case CS_ERR_NULL: return "null pointer argument";
+    case CS_ERR_PADDING: return "nonzero padded output";
+    case CS_ERR_UNSUPPORTED: return "shape not supported by the selected kernel";
+    case CS_ERR_PROBE: return "probe kernel mismatch";
+    case CS_ERR_ARG: return "invalid argument";
+    default: return "unknown error code";
+  }
+}
+
+const char* cs_last_error_detail(void) { return t_detail; }
+
+const char* cs_kernel_name(int kernel) {
+  switch (kernel) {
+    case CS_KERNEL_AUTO: return "auto";
+    case CS_KERNEL_BASELINE: return "baseline";
+    case CS_KERNEL_WARP: return "warp";
+    case CS_KERNEL_TMA: return "tma";
+    case CS_KERNEL_PIPELINE: return "pipeline";
+    case CS_KERNEL_ONLINE: return "online";
+    default: return nullptr;
+  }
+}
+
+int cs_kernel_parse(const char* name) {
+  if (!name) return CS_ERR_BAD_KERNEL;
+  for (int k = CS_KERNEL_AUTO; k <= CS_KERNEL_ONLINE; ++k)
+    if (std::strcmp(name, cs_kernel_name(k)) == 0) return k;
+  return CS_ERR_BAD_KERNEL;
+}
+
+int cs_kernel_supports(int kernel, int64_t cols) {
+  if (!is_known_kernel(kernel)) return 0;
+  return kernel != CS_KERNEL_WARP || cols <= 32;
+}
+
+int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols) {
+  if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
+  if (kernel != CS_KERNEL_AUTO) return kernel;
+  if (cols <= 32) return CS_KERNEL_WARP;
+  // Host-side rule equal to make_plan's: the row-resident kernel takes any
+  // shape whose widest unit fits 576 threads x 8 vectors and two stages.
+  Geometry g{};
+  g.batch = 1;
+  g.rows = (int32_t)std::min<int64_t>(rows, kI32Max);
+  g.cols = (int32_t)std::min<int64_t>(cols, kI32Max);
+  g.pitch = (int32_t)std::min<int64_t>(padded_pitch(cols), kI32Max - 7);
+  const cs::UnitMap m = cs::make_unit_map(g);
+  const int64_t max_nv = rowres_max_vectors(g, m);
+  const int64_t stage = (max_nv * 16 + 127) / 128 * 128;
+  if (max_nv <= 8 * rowres_maxt(8) && 2 * stage + cs::rowres_tail_bytes(2) <= 232448) return CS_KERNEL_TMA;
+  return CS_KERNEL_ONLINE;
+}
+
+double cs_logical_bytes(int kernel, int64_t rows, int64_t cols) {
+  if (!is_known_kernel(kernel) || kernel == CS_KERNEL_AUTO || rows <= 0 || cols <= 0) return -1.0;
+  Geometry g{};
+  g.batch = 1;
+  g.rows = (int32_t)std::min<int64_t>(rows, kI32Max);
+  g.cols = (int32_t)std::min<int64_t>(cols, kI32Max);
+  return modelled_bytes(kernel, g, kOnlineDefaultStages);
+}
+
+double cs_roofline_bytes(int64_t rows, int64_t cols, int64_t row_offset) {
+  if (rows <= 0 || cols <= 0 || row_offset < 0) return 0.0;
+  return 2.0 * causal_elements(rows, cols, row_offset) + 2.0 * (double)rows * (double)cols;
+}
+
+int64_t cs_padded_pitch(int64_t cols) { return padded_pitch(cols); }
+
+int cs_validate(int64_t batch, int64_t batch_stride, int64_t rows, int64_t cols, int64_t pitch,
+                int64_t row_offset, float scale) {
+  return validate_args(batch, batch_stride, rows, cols, pitch, row_offset, scale);
+}
+
+int cs_check_finite_host(const uint16_t* scores, int64_t n) {
+  if (n > 0 && !scores) return CS_ERR_NULL;
+  for (int64_t i = 0; i < n; ++i)
+    if ((scores[i] & 0x7c00u) == 0x7c00u) return CS_ERR_NON_FINITE;
+  return CS_OK;
+}
+
+int cs_device_sm_count(int device) {
+  DeviceInfo* d = nullptr;
+  const int rc = device_info(device, &d);
+  return rc ? rc : d->sms;
+}
+
+int cs_plan_create(cs_plan** plan, int device, const void* d_in, void* d_out, int64_t batch,
+                   int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch, int32_t row_offset) {
+  if (!plan) return CS_ERR_NULL;
+  *plan = nullptr;
+  int rc = validate_args(batch, batch_stride, rows, cols, pitch, row_offset, 1.0f);
+  if (rc) return rc;
+  rc = check_pointers(d_in, d_out);
+  if (rc) return rc;
+  DeviceInfo* d = nullptr;
+  rc = device_info(device, &d);
+  if (rc) return rc;
+  cs_plan* p = new (std::nothrow) cs_plan();
+  if (!p) return CS_ERR_ARG;
+  p->device = device;
+  p->g.in = static_cast<const uint16_t*>(d_in);
+  p->g.out = static_cast<uint16_t*>(d_out);
+  p->g.batch = batch;
+  p->g.batch_stride = batch > 1 ? batch_stride : (int64_t)rows * pitch;
+  p->g.rows = rows;
+  p->g.cols = cols;
+  p->g.pitch = pitch;
+  p->g.row_offset = row_offset;
+  p->g.timeout_ns = kDefaultTimeoutNs;
+  DeviceGuard guard(device);
+  cudaError_t e = cudaMalloc(&p->d_status, 256);
+  if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, 256);
+  if (e != cudaSuccess) {
+    if (p->d_status) cudaFree(p->d_status);
+    delete p;
+    return cuda_fail(e, "plan status word");
+  }
+  p->g.status = p->d_status;
+  *plan = p;
+  return CS_OK;
+}
+
+int cs_plan_set_timeout(cs_plan* plan, uint64_t timeout_ns) {
+  if (!plan) return CS_ERR_NULL;
+  if (timeout_ns == 0) return CS_ERR_ARG;
+  plan->g.timeout_ns = timeout_ns;
+  return CS_OK;
+}
+
+int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint) {
+  if (!plan) return CS_ERR_NULL;
+  if (vec_per_thread != 0 && vec_per_thread != 2 && vec_per_thread != 4 && vec_per_thread != 8)
+    return CS_ERR_ARG;
+  if (stages < 0 || stages > 24 || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
+  plan->tuning.vec = vec_per_thread;
+  plan->tuning.stages = stages;
+  plan->tuning.hint = l2_hint;
+  return CS_OK;
+}
+
+static int plan_launch_impl(cs_plan* plan, int kernel, float scale, void* stream, uint32_t flags,
+                            uint64_t timeout_ns) {
+  if (!plan) return CS_ERR_NULL;
+  if (!std::isfinite(scale) || !(scale >= 0.0f && scale <= CS_MAX_SCALE)) return CS_ERR_BAD_SCALE;
+  Geometry g = plan->g;
+  g.scale = scale;
+  g.flags = flags;
+  if (timeout_ns) g.timeout_ns = timeout_ns;
+  DeviceGuard guard(plan->device);
+  if (!guard.ok()) return CS_ERR_DEVICE;
+  return launch_geometry(plan->device, kernel, g, plan->tuning, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int cs_plan_launch(cs_plan* plan, int kernel, float scale, void* stream) {
+  return plan_launch_impl(plan, kernel, scale, stream, 0u, 0ull);
+}
+
+int cs_plan_launch_debug(cs_plan* plan, int kernel, float scale, void* stream, uint32_t flags,
+                         uint64_t timeout_ns) {
+  return plan_launch_impl(plan, kernel, scale, stream, flags, timeout_ns);
+}
+
+int cs_plan_status(cs_plan* plan, uint32_t* status) {
+  if (!plan) return CS_ERR_NULL;
+  DeviceGuard guard(plan->device);
+  CS_CUDA(cudaDeviceSynchronize());
+  uint32_t s = 0;
+  CS_CUDA(cudaMemcpy(&s, plan->d_status, sizeof s, cudaMemcpyDeviceToHost));
+  CS_CUDA(cudaMemset(plan->d_status, 0, sizeof s));
+  if (status) *status = s;
+  return (s & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
+}
+
+int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
+  if (!plan || !info) return CS_ERR_NULL;
+  DeviceInfo* d = nullptr;
+  DeviceGuard guard(plan->device);
+  int rc = device_info(plan->device, &d);
+  if (rc) return rc;
+  LaunchPlan lp;
+  rc = make_plan(*d, kernel, plan->g, plan->tuning, &lp);
+  if (rc) return rc;
+  std::memset(info, 0, sizeof *info);
+  info->kernel = lp.kernel;
+  info->grid = lp.grid;
+  info->block = lp.block;
+  info->smem_bytes = lp.smem;
+  info->stages = lp.stages;
+  info->vec_per_thread = lp.vec;
+  info->ctas_per_sm = lp.ctas_per_sm;
+  info->launches = 1;
+  info->units = lp.units;
+  info->algorithmic_bytes =
+      cs_roofline_bytes(plan->g.rows, plan->g.cols, plan->g.row_offset) * (double)plan->g.batch;
+  info->modelled_bytes = modelled_bytes(lp.kernel, plan->g, lp.stages ? lp.stages : kOnlineDefaultStages);
+  return CS_OK;
+}
+
+void cs_plan_destroy(cs_plan* plan) {
+  if (!plan) return;
+  {
+    DeviceGuard guard(plan->device);
+    if (plan->d_status) cudaFree(plan->d_status);
+  }
+  delete plan;
+}
+
+int cs_softmax_batched(int kernel, const void* d_in, void* d_out, int64_t batch, int64_t batch_stride,
+                       int32_t rows, int32_t cols, int32_t pitch, int32_t row_offset, float scale,
+                       void* stream) {
+  int rc = validate_args(batch, batch_stride, rows, cols, pitch, row_offset, scale);
+  if (rc) return rc;
+  rc = check_pointers(d_in, d_out);
+  if (rc) return rc;
+  if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
+  int dev = 0;
+  CS_CUDA(cudaGetDevice(&dev));
+  uint32_t* status = nullptr;
+  rc = status_word_for(dev, &status);
+  if (rc) return rc;
+  Geometry g{};
+  g.in = static_cast<const uint16_t*>(d_in);
+  g.out = static_cast<uint16_t*>(d_out);
+  g.batch = batch;
+  g.batch_stride = batch > 1 ? batch_stride : (int64_t)rows * pitch;
+  g.rows = rows;
+  g.cols = cols;
+  g.pitch = pitch;
+  g.row_offset = row_offset;
+  g.scale = scale;
+  g.status = status;
+  g.timeout_ns = kDefaultTimeoutNs;
+  return launch_geometry(dev, kernel, g, Tuning{}, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int cs_softmax(int kernel, const void* d_in, void* d_out, int32_t rows, int32_t cols, int32_t pitch,
+               float scale, void* stream) {
+  return cs_softmax_batched(kernel, d_in, d_out, 1, 0, rows, cols, pitch, 0, scale, stream);
+}
+
+// ===========================================================================
+// Sessions
+// ===========================================================================
+
+int cs_session_create(cs_session** session, int device) {
+  if (!session) return CS_ERR_NULL;
+  *session = nullptr;
+  DeviceInfo* d = nullptr;
+  int rc = device_info(device, &d);
+  if (rc) return rc;
+  DeviceGuard guard(device);
+  cs_session* s = new (std::nothrow) cs_session();
+  if (!s) return CS_ERR_ARG;
+  s->device = device;
+  cudaError_t e = cudaStreamCreateWithFlags(&s->streams[0], cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->streams[1], cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&s->d_status, 256);
+  if (e == cudaSuccess) e = cudaMemset(s->d_status, 0, 256);
+  if (e == cudaSuccess) e = cudaMalloc(&s->d_counter, sizeof(unsigned long long));
+  if (e != cudaSuccess) {
+    cs_session_destroy(s);
+    return cuda_fail(e, "session setup");
+  }
+  *session = s;
+  return CS_OK;
+}
+
+void* cs_session_stream(cs_session* session) { return session ? session->streams[0] : nullptr; }
+
+int cs_session_probe(cs_session* session) {
+  if (!session) return CS_ERR_NULL;
+  DeviceGuard guard(session->device);
+  uint32_t* d = nullptr;
+  CS_CUDA(cudaMalloc(&d, 256 * sizeof(uint32_t)));
+  cs::probe_kernel<<<1, 256, 0, session->streams[0]>>>(d, 256);
+  uint32_t h[256];
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h, d, sizeof h, cudaMemcpyDeviceToHost, session->streams[0]);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(session->streams[0]);
+  cudaFree(d);
+  if (e != cudaSuccess) return cuda_fail(e, "probe");
+  for (int i = 0; i < 256; ++i)
+    if (h[i] != ((uint32_t)i ^ 0x5a5a5a5au)) {
+      std::snprintf(t_detail, sizeof t_detail, "probe mismatch at %d", i);
+      return CS_ERR_PROBE;
+    }
+  return CS_OK;
+}
+
+static int session_read_status(cs_session* s) {
+  uint32_t st = 0;
+  CS_CUDA(cudaMemcpy(&st, s->d_status, sizeof st, cudaMemcpyDeviceToHost));
+  if (st) CS_CUDA(cudaMemset(s->d_status, 0, sizeof st));
+  return (st & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
+}
+
+int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
+                            int64_t batch, int32_t rows, int32_t cols, float scale) {
+  if (!session || !h_in || !h_out) return CS_ERR_NULL;
+  const int64_t pitch = padded_pitch(cols);
+  int rc = validate_args(batch, (int64_t)rows * pitch, rows, cols, pitch, 0, scale);
+  if (rc) return rc;
+  if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
+  DeviceGuard guard(session->device);
+  const size_t mat_dev = (size_t)rows * (size_t)pitch * 2;
+  const size_t mat_host = (size_t)rows * (size_t)cols * 2;
+  // Chunks of about 256 MB alternate between two streams/slots.
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(batch, (int64_t)((256u << 20) / mat_dev)));
+  const size_t need = (size_t)chunk * mat_dev;
+  if (need > session->slot_bytes) {
+    for (int i = 0; i < 2; ++i) {
+      if (session->d_in[i]) cudaFree(session->d_in[i]);
+      if (session->d_out[i]) cudaFree(session->d_out[i]);
+      session->d_in[i] = session->d_out[i] = nullptr;
+    }
+    session->slot_bytes = 0;
+    for (int i = 0; i < 2; ++i) {
+      CS_CUDA(cudaMalloc(&session->d_in[i], need));
+      CS_CUDA(cudaMalloc(&session->d_out[i], need));
+    }
+    session->slot_bytes = need;
+  }
+  const size_t dpitch = (size_t)pitch * 2, hpitch = (size_t)cols * 2;
+  for (int64_t c0 = 0, it = 0; c0 < batch; c0 += chunk, ++it) {
+    const int slot = (int)(it & 1);
+    cudaStream_t st = session->streams[slot];
+    const int64_t n = std::min<int64_t>(chunk, batch - c0);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(h_in) + (size_t)c0 * mat_host;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(h_out) + (size_t)c0 * mat_host;
+    if (pitch == cols)
+      CS_CUDA(cudaMemcpyAsync(session->d_in[slot], src, (size_t)n * mat_host, cudaMemcpyHostToDevice, st));
+    else
+      CS_CUDA(cudaMemcpy2DAsync(session->d_in[slot], dpitch, src, hpitch, hpitch, (size_t)n * rows,
+                                cudaMemcpyHostToDevice, st));
+    Geometry g{};
+    g.in = session->d_in[slot];
+    g.out = session->d_out[slot];
+    g.batch = n;
+    g.batch_stride = (int64_t)rows * pitch;
+    g.rows = rows;
+    g.cols = cols;
+    g.pitch = (int32_t)pitch;
+    g.row_offset = 0;
+    g.scale = scale;
+    g.status = session->d_status;
+    g.timeout_ns = kDefaultTimeoutNs;
+    rc = launch_geometry(session->device, kernel, g, Tuning{}, st, nullptr);
+    if (rc) {
+      cudaStreamSynchronize(session->streams[0]);
+      cudaStreamSynchronize(session->streams[1]);
+      return rc;
+    }
+    if (pitch == cols)
+      CS_CUDA(cudaMemcpyAsync(dst, session->d_out[slot], (size_t)n * mat_host, cudaMemcpyDeviceToHost, st));
+    else
+      CS_CUDA(cudaMemcpy2DAsync(dst, hpitch, session->d_out[slot], dpitch, hpitch, (size_t)n * rows,
+                                cudaMemcpyDeviceToHost, st));
+  }
+  CS_CUDA(cudaStreamSynchronize(session->streams[0]));
+  CS_CUDA(cudaStreamSynchronize(session->streams[1]));
+  return session_read_status(session);
+}
+
+int cs_session_prepare(cs_session* session, const uint16_t* h_in, int32_t rows, int32_t cols) {
+  if (!session || !h_in) return CS_ERR_NULL;
+  const int64_t pitch = padded_pitch(cols);
+  int rc = validate_args(1, 0, rows, cols, pitch, 0, 1.0f);
+  if (rc) return rc;
+  DeviceGuard guard(session->device);
+  const size_t bytes = (size_t)rows * (size_t)pitch * 2;
+  if (bytes > session->p_bytes) {
+    if (session->p_in) cudaFree(session->p_in);
+    if (session->p_out) cudaFree(session->p_out);
+    session->p_in = session->p_out = nullptr;
+    session->p_bytes = 0;
+    CS_CUDA(cudaMalloc(&session->p_in, bytes));
+    CS_CUDA(cudaMalloc(&session->p_out, bytes));
+    session->p_bytes = bytes;
+  }
+  cudaStream_t st = session->streams[0];
+  // gpu/src/driver.rs:75-79: zero padding on the input, sentinel 0xfb00 on the output.
+  CS_CUDA(cudaMemsetAsync(session->p_in, 0, bytes, st));
+  CS_CUDA(cudaMemcpy2DAsync(session->p_in, (size_t)pitch * 2, h_in, (size_t)cols * 2, (size_t)cols * 2,
+                            (size_t)rows, cudaMemcpyHostToDevice, st));
+  const int64_t n = (int64_t)rows * pitch;
+  cs::fill_u16_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, st>>>(session->p_out, n, 0xfb00u);
+  CS_CUDA(cudaGetLastError());
+  CS_CUDA(cudaStreamSynchronize(st));
+  session->p_rows = rows;
+  session->p_cols = cols;
+  session->p_pitch = (int32_t)pitch;
+  session->prepared = true;
+  return CS_OK;
+}
+
+int cs_session_launch(cs_session* session, int kernel, float scale) {
+  if (!session) return CS_ERR_NULL;
+  if (!session->prepared) return CS_ERR_ARG;
+  if (!std::isfinite(scale) || !(scale >= 0.0f && scale <= CS_MAX_SCALE)) return CS_ERR_BAD_SCALE;
+  DeviceGuard guard(session->device);
+  Geometry g{};
+  g.in = session->p_in;
+  g.out = session->p_out;
+  g.batch = 1;
+  g.batch_stride = (int64_t)session->p_rows * session->p_pitch;
+  g.rows = session->p_rows;
+  g.cols = session->p_cols;
+  g.pitch = session->p_pitch;
+  g.scale = scale;
+  g.status = session->d_status;
+  g.timeout_ns = kDefaultTimeoutNs;
+  return launch_geometry(session->device, kernel, g, Tuning{}, session->streams[0], nullptr);
+}
+
+int cs_session_result(cs_session* session, uint16_t* h_out) {
+  if (!session || !h_out) return CS_ERR_NULL;
+  if (!session->prepared) return CS_ERR_ARG;
+  DeviceGuard guard(session->device);
+  cudaStream_t st = session->streams[0];
+  CS_CUDA(cudaStreamSynchronize(st));
+  int rc = session_read_status(session);
+  if (rc) return rc;
+  const int32_t rows = session->p_rows, cols = session->p_cols, pitch = session->p_pitch;
+  if (pitch > cols) {
+    CS_CUDA(cudaMemsetAsync(session->d_counter, 0, sizeof(unsigned long long), st));
+    const int64_t n = (int64_t)rows * (pitch - cols);
+    cs::padding_check_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, st>>>(
+        session->p_out, rows, cols, pitch, session->d_counter);
+    CS_CUDA(cudaGetLastError());
+    unsigned long long bad = 0;
+    CS_CUDA(cudaMemcpyAsync(&bad, session->d_counter, sizeof bad, cudaMemcpyDeviceToHost, st));
+    CS_CUDA(cudaStreamSynchronize(st));
+    if (bad) {
+      std::snprintf(t_detail, sizeof t_detail, "%llu nonzero padded outputs", bad);
+      return CS_ERR_PADDING;
+    }
+  }
+  CS_CUDA(cudaMemcpy2DAsync(h_out, (size_t)cols * 2, session->p_out, (size_t)pitch * 2, (size_t)cols * 2,
+                            (size_t)rows, cudaMemcpyDeviceToHost, st));
+  CS_CUDA(cudaStreamSynchronize(st));
+  return CS_OK;
+}
+
+void cs_session_destroy(cs_session* session) {
+  if (!session) return;
+  {
+    DeviceGuard guard(session->device);
+    for (int i = 0; i < 2; ++i) {
+      if (session->streams[i]) cudaStreamSynchronize(session->streams[i]);
+    }
+    for (int i = 0; i < 2; ++i) {
+      if (session->d_in[i]) cudaFree(session->d_in[i]);
+      if (session->d_out[i]) cudaFree(session->d_out[i]);
+      if (session->streams[i]) cudaStreamDestroy(session->streams[i]);
+    }
+    if (session->p_in) cudaFree(session->p_in);
+    if (session->p_out) cudaFree(session->p_out);
+    if (session->d_status) cudaFree(session->d_status);
+    if (session->d_counter) cudaFree(session->d_counter);
+  }
+  delete session;
+}
+
+int cs_host_register(void* ptr, size_t bytes) {
+  if (!ptr) return CS_ERR_NULL;
+  CS_CUDA(cudaHostRegister(ptr, bytes, cudaHostRegisterDefault));
+  return CS_OK;
+}
+
+int cs_host_unregister(void* ptr) {
+  if (!ptr) return CS_ERR_NULL;
+  CS_CUDA(cudaHostUnregister(ptr));
+  return CS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,260 @@
+/*
+ * causal_softmax.h — C ABI of the B200 (sm_100a) fused causal softmax.
+ *
+ *   P[r,c] = exp(scale*S[r,c] - max_r) / sum_{j<=r} exp(scale*S[r,j] - max_r)   for c <= r
+ *   P[r,c] = +0.0 (bit pattern 0x0000)                                         otherwise
+ *
+ * S and P are IEEE binary16 stored as uint16_t bits, row-major with a row
+ * pitch (elements) that is a multiple of 8, so every row starts 16-byte
+ * aligned; arithmetic is binary32. The masked upper triangle is never read,
+ * and every output column the softmax does not own — including the pitch
+ * padding — is written 0x0000.
+ *
+ * Every entry point stands in for a piece of the reference project's host
+ * surface (R-P-Padhi/GB200-SM100A-TMA-Fused-Causal-Attention-Softmax; file:line
+ * citations below are paths inside that project). Plain pointers and sizes
+ * only: device pointers are CUDA device addresses, `stream` is a
+ * cudaStream_t passed as void*. Functions return 0 (CS_OK) or a negative
+ * CS_ERR_* code; none of them allocates or frees caller buffers.
+ *
+ * Threads: distinct plans and sessions may be used from different host
+ * threads concurrently; one plan or session must not be used by two threads
+ * at once.
+ */
+#ifndef CAUSAL_SOFTMAX_H
+#define CAUSAL_SOFTMAX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CS_ABI_VERSION 1
+
+/* Kernel selection. Mirrors host/src/lib.rs:5-13 (enum Kernel) and the names
+ * host/src/lib.rs:22-42 parses; each name selects this library's design:
+ *   BASELINE : one CTA per row, three passes over global memory (control)
+ *   WARP     : narrow rows, one 16-byte vector per lane (cols <= 32)
+ *   TMA      : row-resident single pass, TMA bulk-copy ring, thread stores
+ *   PIPELINE : as TMA, with TMA bulk stores of the output
+ *   ONLINE   : pipelined online-softmax over 8 KB tiles for long rows
+ *   AUTO     : resolved by cs_resolve_kernel */
+typedef enum cs_kernel {
+    CS_KERNEL_AUTO = 0,
+    CS_KERNEL_BASELINE = 1,
+    CS_KERNEL_WARP = 2,
+    CS_KERNEL_TMA = 3,
+    CS_KERNEL_PIPELINE = 4,
+    CS_KERNEL_ONLINE = 5
+} cs_kernel;
+
+/* Error codes. -1..-4 mirror reference/src/lib.rs:8-27 (ShapeError); the
+ * warp-width error mirrors gpu/src/driver.rs:149-151; the alignment/pitch
+ * errors mirror the tensor_map checks gpu/src/main.rs:737-742; the size
+ * limits mirror host/src/lib.rs:143-168 (Config::validate). */
+enum {
+    CS_OK = 0,
+    CS_ERR_EMPTY = -1,          /* matrix dimensions must be positive */
+    CS_ERR_WRONG_LENGTH = -2,   /* sizes overflow or buffer/stride too small */
+    CS_ERR_BAD_SCALE = -3,      /* scale must be finite and in [0, 1e30] */
+    CS_ERR_NON_FINITE = -4,     /* score matrix contains NaN or infinity */
+    CS_ERR_WARP_COLS = -5,      /* warp specialization requires cols <= 32 */
+    CS_ERR_ALIGNMENT = -6,      /* base pointer not 16-byte aligned */
+    CS_ERR_PITCH = -7,          /* pitch < cols, not a multiple of 8, or too large */
+    CS_ERR_BAD_KERNEL = -8,     /* unknown kernel */
+    CS_ERR_DEVICE = -9,         /* no usable sm_100 device */
+    CS_ERR_CUDA = -10,          /* a CUDA runtime call failed */
+    CS_ERR_TIMEOUT = -11,       /* a bounded device-side wait ran out */
+    CS_ERR_NULL = -12,          /* null pointer argument */
+    CS_ERR_PADDING = -13,       /* nonzero padded output found */
+    CS_ERR_UNSUPPORTED = -14,   /* shape beyond the selected kernel's limits */
+    CS_ERR_PROBE = -15,         /* probe kernel returned a wrong value */
+    CS_ERR_ARG = -16            /* other invalid argument */
+};
+
+#define CS_MAX_SCALE 1.0e30f   /* reference/src/lib.rs:5 */
+
+/* Device status word bits reported by cs_plan_status. */
+#define CS_STATUS_TIMEOUT 1u
+#define CS_STATUS_BAD_UNIT 2u
+
+/* ---------------------------------------------------------------- */
+/* Host-only queries (no GPU needed)                                 */
+/* ---------------------------------------------------------------- */
+
+int cs_abi_version(void);
+
+/* Static message for a CS_* code; never NULL. */
+const char *cs_strerror(int code);
+
+/* Detail of the last error raised on the calling thread (CUDA error text,
+ * offending size); empty if none. Thread-local storage, never NULL. */
+const char *cs_last_error_detail(void);
+
+/* host/src/lib.rs:22-31 (Kernel::name). NULL for an unknown value. */
+const char *cs_kernel_name(int kernel);
+
+/* host/src/lib.rs:32-42 (Kernel::parse). Returns the cs_kernel value or CS_ERR_BAD_KERNEL. */
+int cs_kernel_parse(const char *name);
+
+/* host/src/lib.rs:43-45 (Kernel::supports): 1 if `kernel` accepts `cols`, else 0. */
+int cs_kernel_supports(int kernel, int64_t cols);
+
+/* host/src/lib.rs:169-177 (Config::resolved_kernel) for this library:
+ * WARP for cols <= 32, TMA while a row pair fits the row-resident kernel,
+ * ONLINE beyond. Non-AUTO values are returned unchanged. */
+int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols);
+
+/* host/src/lib.rs:49-64 (Kernel::logical_bytes) for this library's kernels:
+ * modelled HBM bytes of one matrix (read traffic of each kernel + one write
+ * of the full rows x cols output). Returns a negative value for AUTO or an
+ * unknown kernel. */
+double cs_logical_bytes(int kernel, int64_t rows, int64_t cols);
+
+/* Algorithmic bytes of one matrix: 2*T + 2*rows*cols, T = causal element
+ * count of rows [row_offset, row_offset+rows) (host/src/lib.rs:52-56 for
+ * row_offset 0). The roofline every kernel is measured against. */
+double cs_roofline_bytes(int64_t rows, int64_t cols, int64_t row_offset);
+
+/* reference/src/lib.rs:132-134: pitch = round_up(cols, 8). */
+int64_t cs_padded_pitch(int64_t cols);
+
+/* Argument checks every launch performs (reference/src/lib.rs:110-129 for
+ * shape and scale, host/src/lib.rs:143-168 for the size limits,
+ * gpu/src/main.rs:737-742 for the pitch rule). batch_stride is ignored when
+ * batch == 1. Does not inspect data (see cs_check_finite_host). */
+int cs_validate(int64_t batch, int64_t batch_stride, int64_t rows, int64_t cols, int64_t pitch,
+                int64_t row_offset, float scale);
+
+/* reference/src/lib.rs:125-127: CS_ERR_NON_FINITE if any of `n` halves is
+ * NaN or infinite, else CS_OK. */
+int cs_check_finite_host(const uint16_t *scores, int64_t n);
+
+/* ---------------------------------------------------------------- */
+/* Device path: plans (replaces gpu/src/driver.rs:65-211)            */
+/* ---------------------------------------------------------------- */
+
+typedef struct cs_plan cs_plan;
+
+/* Describe a launch target once: `batch` matrices at d_in/d_out (element
+ * stride batch_stride between matrices), each `rows` x `cols` with row pitch
+ * `pitch`; local row i is absolute causal row row_offset + i (row-block
+ * shards). Replaces Session::prepare_on + tensor_map (gpu/src/driver.rs:65-95,
+ * gpu/src/main.rs:730-774): the plan keeps the launch geometry and a 256-byte
+ * device status word (the only allocation it makes). The caller keeps
+ * ownership of d_in/d_out, which may alias only if d_in == d_out is NOT used
+ * (in-place is not supported). */
+int cs_plan_create(cs_plan **plan, int device, const void *d_in, void *d_out, int64_t batch,
+                   int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch,
+                   int32_t row_offset);
+
+/* Enqueue the softmax on `stream` (replaces Session::launch_on,
+ * gpu/src/driver.rs:108-211). Asynchronous: no host synchronisation and no
+ * allocation. Errors: argument errors as cs_validate, CS_ERR_WARP_COLS,
+ * CS_ERR_UNSUPPORTED, CS_ERR_CUDA. */
+int cs_plan_launch(cs_plan *plan, int kernel, float scale, void *stream);
+
+/* Synchronise the plan's device and read (then clear) its status word.
+ * *status receives the CS_STATUS_* bits; returns CS_ERR_TIMEOUT if the
+ * timeout bit was set, CS_OK otherwise. */
+int cs_plan_status(cs_plan *plan, uint32_t *status);
+
+/* Bound, in nanoseconds of GPU time, on every device-side wait of later
+ * launches of this plan (default 2 s). */
+int cs_plan_set_timeout(cs_plan *plan, uint64_t timeout_ns);
+
+/* Tuning knobs for the TMA / PIPELINE kernels (0 = automatic):
+ * vectors per thread (2, 4 or 8), ring stages (1..16), L2 evict-first hint
+ * on the input copies (0 off, 1 on, -1 automatic). */
+int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint);
+
+typedef struct cs_launch_info {
+    int32_t kernel;          /* resolved cs_kernel */
+    int32_t grid;            /* CTAs per launch */
+    int32_t block;           /* threads per CTA */
+    int32_t smem_bytes;      /* dynamic shared memory per CTA */
+    int32_t stages;          /* ring depth (TMA/PIPELINE/ONLINE), else 0 */
+    int32_t vec_per_thread;  /* TMA/PIPELINE registers: 16-byte vectors per thread */
+    int32_t ctas_per_sm;     /* resident CTAs per SM from the occupancy query */
+    int32_t launches;        /* kernel launches per cs_plan_launch (always 1) */
+    int64_t units;           /* work units (row pairs, rows) per launch */
+    double algorithmic_bytes;/* roofline bytes per launch (all matrices) */
+    double modelled_bytes;   /* the kernel's own modelled HBM bytes per launch */
+} cs_launch_info;
+
+/* Launch geometry a cs_plan_launch with `kernel` would use. */
+int cs_plan_describe(cs_plan *plan, int kernel, cs_launch_info *info);
+
+/* Test hook: launch with debug flags (1 = the producer issues no copies, so
+ * every consumer wait must run out after `timeout_ns` and report
+ * CS_STATUS_TIMEOUT). Not for production use. */
+int cs_plan_launch_debug(cs_plan *plan, int kernel, float scale, void *stream, uint32_t flags,
+                         uint64_t timeout_ns);
+
+void cs_plan_destroy(cs_plan *plan);
+
+/* One-shot launches on the current device (no plan object). The status word
+ * is a per-device buffer the library allocates on the first call for that
+ * device. cs_softmax has the argument meaning of the reference's kernel
+ * launches (gpu/src/main.rs:72-78: input, output, cols, pitch, scale). */
+int cs_softmax(int kernel, const void *d_in, void *d_out, int32_t rows, int32_t cols,
+               int32_t pitch, float scale, void *stream);
+
+int cs_softmax_batched(int kernel, const void *d_in, void *d_out, int64_t batch,
+                       int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch,
+                       int32_t row_offset, float scale, void *stream);
+
+/* ---------------------------------------------------------------- */
+/* Sessions: host buffers (replaces gpu/src/driver.rs:12-59, 213-248) */
+/* ---------------------------------------------------------------- */
+
+typedef struct cs_session cs_session;
+
+/* Bind a device (requires compute capability 10.x, gpu/src/driver.rs:29-42)
+ * and create the session's streams. */
+int cs_session_create(cs_session **session, int device);
+
+/* gpu/src/driver.rs:44-59: run the probe kernel (out[i] = i ^ 0x5a5a5a5a
+ * over 256 lanes) and check every lane. CS_ERR_PROBE on a mismatch. */
+int cs_session_probe(cs_session *session);
+
+/* End to end from host memory: `batch` dense rows x cols matrices (no
+ * padding, like reference/src/lib.rs:85) are copied to the device with the
+ * padded pitch, softmaxed, and copied back unpadded into h_out. Chunks of
+ * matrices alternate between two streams so host->device copies, kernels and
+ * device->host copies overlap; device buffers are cached in the session.
+ * Pinned host memory (cs_host_register) makes the copies asynchronous.
+ * Returns after the last copy has landed; checks the status word. */
+int cs_session_softmax_host(cs_session *session, int kernel, const uint16_t *h_in,
+                            uint16_t *h_out, int64_t batch, int32_t rows, int32_t cols,
+                            float scale);
+
+/* The reference's prepare / launch / result cycle (gpu/src/driver.rs:65-95,
+ * 108-211, 213-232) for one matrix: prepare copies `h_in` (dense rows x cols)
+ * into a padded device buffer and fills the output with the 0xfb00
+ * sentinel; launch runs `kernel`; result synchronises, checks that the
+ * padding columns are zero (CS_ERR_PADDING) and copies the unpadded output
+ * to h_out. */
+int cs_session_prepare(cs_session *session, const uint16_t *h_in, int32_t rows, int32_t cols);
+int cs_session_launch(cs_session *session, int kernel, float scale);
+int cs_session_result(cs_session *session, uint16_t *h_out);
+
+/* The session's primary stream (cudaStream_t as void*). */
+void *cs_session_stream(cs_session *session);
+
+void cs_session_destroy(cs_session *session);
+
+/* Page-lock / release caller host memory for asynchronous copies. */
+int cs_host_register(void *ptr, size_t bytes);
+int cs_host_unregister(void *ptr);
+
+/* Number of SMs of `device` (for grid sizing by callers), or a CS_ERR_* code. */
+int cs_device_sm_count(int device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAUSAL_SOFTMAX_H */

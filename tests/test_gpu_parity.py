@@ -1,0 +1,351 @@
+"""GPU parity tests: every kernel, called through the C ABI, against the CPU oracle.
+
+Shapes and patterns follow the reference's hardware suites
+(gpu/src/driver.rs:250-331: QUICK x {zeros, spikes, random} at scale 0.125, and
+MORE x all seven patterns x scales {0, 0.125, 0.5, 1, 1e30}), plus the five
+benchmark configurations and the row-block / batch layouts this library adds.
+Outputs start filled with the 0xfb00 sentinel (gpu/src/driver.rs:78-79), so a
+missing store shows up as a mask or element violation.
+
+Tolerances (see gpu_helpers): masked == 0x0000 bit-exact; unmasked within
+2 FP16 ulp or 2e-3 absolute of the FP64 oracle rounded to half; |row sum - 1|
+<= 2e-3; and the reference verifier (0.003 + 0.003*w, row sum 0.02) accepts.
+"""
+import numpy as np
+import pytest
+import torch
+
+import causal_softmax as cs
+import oracle_ctypes as O
+from gpu_helpers import (KERNELS, SENTINEL, check, from_dev, pattern_input, run, sentinel_like,
+                         supported, to_dev)
+
+pytestmark = pytest.mark.gpu
+
+# gpu/src/driver.rs:250-265
+QUICK = [(1, 1), (1, 8), (2, 17), (3, 31), (4, 32), (5, 33), (7, 64), (8, 127), (9, 256),
+         (10, 257), (13, 513), (17, 1024), (33, 9), (64, 65)]
+# gpu/src/driver.rs:266-285
+MORE = [(1, 129), (2, 255), (3, 256), (4, 257), (5, 511), (6, 512), (7, 513), (8, 1025),
+        (15, 2048), (16, 16), (31, 31), (32, 32), (33, 33), (64, 128), (65, 256), (127, 512),
+        (129, 8192), (257, 257)]
+STRESS_SCALES = [0.0, 0.125, 0.5, 1.0, 1.0e30]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    import build
+
+    build.build_library()
+    assert torch.cuda.is_available()
+    major, _ = torch.cuda.get_device_capability(0)
+    assert major == 10, "these kernels are built for sm_100a only"
+    yield
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_gpu_tests_quick(kernel):
+    n = 0
+    for rows, cols in QUICK:
+        if not supported(kernel, cols):
+            continue
+        for pattern in ("zeros", "spikes", "random"):
+            x = pattern_input(rows, cols, pattern)
+            got = run(kernel, x, cols=cols, scale=0.125)
+            check(got, x, cols=cols, scale=0.125, what=f"{kernel} {rows}x{cols} {pattern}")
+            n += 1
+    assert n > 0
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_gpu_stress(kernel):
+    for rows, cols in MORE:
+        if not supported(kernel, cols):
+            continue
+        for pattern in cs.PATTERNS:
+            x = pattern_input(rows, cols, pattern)
+            for scale in STRESS_SCALES:
+                got = run(kernel, x, cols=cols, scale=scale)
+                check(got, x, cols=cols, scale=scale, what=f"{kernel} {rows}x{cols} {pattern} {scale}")
+
+
+@pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online"])
+def test_tall_wide_and_ragged_shapes(kernel):
+    # Rows past the diagonal (M > N), a single row, and widths straddling every
+    # vector / warp / tile boundary of the kernels (8, 256, 512, 4096 columns).
+    for rows, cols in [(300, 64), (1000, 40), (1, 4096), (2, 8191), (40, 4097), (513, 511),
+                       (4100, 33), (97, 4104)]:
+        x = cs.generate(2, 1, batch=1, rows=rows, cols=cols)[0]
+        for scale in (0.0, 0.0883883, 1.0):
+            got = run(kernel, x, cols=cols, scale=scale)
+            check(got, x, cols=cols, scale=scale, what=f"{kernel} {rows}x{cols} {scale}")
+
+
+def test_reference_online_model_shapes_all_kernels():
+    # reference/src/online.rs:79-100 shapes and scales, every kernel.
+    for rows, cols in [(1, 1), (7, 17), (9, 129), (65, 257), (137, 259), (257, 513)]:
+        dense = np.array([O.h(((i * 7919 % 251) - 125.0) * 0.125) for i in range(rows * cols)],
+                         np.uint16)
+        x = O.pad(dense, rows, cols).reshape(rows, cs.padded_pitch(cols))
+        for kernel in KERNELS:
+            if not supported(kernel, cols):
+                continue
+            for scale in (0.0, 0.001, 0.125, 1.0, 10.0):
+                got = run(kernel, x, cols=cols, scale=scale)
+                check(got, x, cols=cols, scale=scale, what=f"{kernel} {rows}x{cols} {scale}")
+                if scale == 0.0:
+                    # Zero scale is an exact uniform distribution (online.rs:116-120).
+                    g = got.reshape(rows, -1)
+                    for r in range(rows):
+                        v = min(r + 1, cols)
+                        assert np.all(g[r, :v] == O.h(1.0 / v)), (kernel, r)
+
+
+@pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online"])
+def test_config1_4096(kernel):
+    x = cs.generate(1, 0, batch=1, rows=4096, cols=4096)[0]
+    got = run(kernel, x, cols=4096, scale=1 / np.sqrt(128))
+    rep = check(got, x, cols=4096, scale=float(np.float32(1 / np.sqrt(128))), what=f"C1 {kernel}")
+    assert rep["max_ulp_vs_f32_spec"] <= 2
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_config2_odd_and_narrow(kernel):
+    for rows, cols, pitch in [(1000, 1037, 1040), (4096, 32, 32)]:
+        if not supported(kernel, cols):
+            continue
+        x = cs.generate(2, 1, batch=1, rows=rows, cols=cols, pitch=pitch)[0]
+        for scale in (0.0, 0.0883883, 1.0):
+            got = run(kernel, x, cols=cols, scale=scale)
+            check(got, x, cols=cols, scale=scale, what=f"C2 {kernel} {rows}x{cols} {scale}")
+            assert np.all(got[:, cols:] == 0)  # padding written zero
+
+
+@pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online"])
+def test_config3_8192_stress(kernel):
+    x = cs.generate(3, 2, batch=1, rows=8192, cols=8192)[0]
+    got = run(kernel, x, cols=8192, scale=1.0)
+    check(got, x, cols=8192, scale=1.0, what=f"C3 {kernel}")
+
+
+def gpu_structure(y: torch.Tensor, cols: int, row_offset: int = 0, chunk: int = 2048) -> dict:
+    """Size-independent properties on the device: masked entries are 0x0000,
+    valid ones finite and non-negative, |row sum - 1| <= 2e-3 (f64 sums)."""
+    y3 = y if y.dim() == 3 else y.unsqueeze(0)
+    batch, rows, pitch = y3.shape
+    col = torch.arange(pitch, device=y.device)
+    worst, bad_mask, bad_val = 0.0, 0, 0
+    for b in range(batch):
+        for r0 in range(0, rows, chunk):
+            blk = y3[b, r0:r0 + chunk]
+            n = blk.shape[0]
+            valid = torch.clamp(torch.arange(r0, r0 + n, device=y.device) + row_offset + 1, max=cols)
+            masked = col[None, :] >= valid[:, None]
+            bits = blk.view(torch.int16)
+            bad_mask += int(((bits != 0) & masked).sum())
+            neg_or_inf = (bits < 0) | ((bits & 0x7C00) == 0x7C00)
+            bad_val += int((neg_or_inf & ~masked).sum())
+            sums = blk.double().sum(dim=1)
+            worst = max(worst, float((sums - 1.0).abs().max()))
+    return {"mask": bad_mask, "values": bad_val, "max_rowsum_err": worst}
+
+
+def test_config4_batched_multihead():
+    # 8 x 32 x 4096^2 = 256 matrices, 8 GiB in + 8 GiB out.
+    free, _ = torch.cuda.mem_get_info()
+    if free < 20 * 2**30:
+        pytest.skip("needs 20 GiB of free device memory")
+    batch, L = 256, 4096
+    scale = float(np.float32(1 / np.sqrt(128)))
+    x = torch.empty((batch, L, L), dtype=torch.int16)
+    cs.generate(4, 3, batch=batch, rows=L, cols=L, out=x.numpy().view(np.uint16))
+    d_in = x.cuda().view(torch.float16)
+    d_out = sentinel_like(d_in)
+    with cs.Plan.for_tensors(d_in, d_out, cols=L) as plan:
+        plan.launch("auto", scale)
+        assert plan.status() == (0, 0)
+    rep = gpu_structure(d_out, L)
+    assert rep["mask"] == 0 and rep["values"] == 0 and rep["max_rowsum_err"] <= 2e-3, rep
+    # Full oracle check on three matrices, and batch invariance (a single-matrix
+    # launch gives the same bits as that matrix inside the batched launch).
+    for b in (0, 137, 255):
+        xb = x[b].numpy().view(np.uint16)
+        gb = from_dev(d_out[b])
+        check(gb, xb, cols=L, scale=scale, what=f"C4 matrix {b}")
+        assert np.array_equal(run("auto", xb, cols=L, scale=scale), gb)
+
+
+def test_config5_long_context():
+    L = 32768
+    free, _ = torch.cuda.mem_get_info()
+    if free < 8 * 2**30:
+        pytest.skip("needs 8 GiB of free device memory")
+    scale = float(np.float32(1 / np.sqrt(128)))
+    x = cs.generate(5, 4, batch=1, rows=L, cols=L)[0]
+    d_in = to_dev(x)
+    for kernel in ("auto", "online"):
+        d_out = sentinel_like(d_in)
+        with cs.Plan.for_tensors(d_in, d_out, cols=L) as plan:
+            plan.launch(kernel, scale)
+            assert plan.status() == (0, 0)
+        rep = gpu_structure(d_out, L)
+        assert rep["mask"] == 0 and rep["values"] == 0 and rep["max_rowsum_err"] <= 2e-3, rep
+        got = from_dev(d_out)
+        # Oracle on row blocks across the matrix (first, middle, last, pair partners).
+        for r0, n in ((0, 64), (8190, 4), (16380, 8), (24570, 4), (L - 64, 64)):
+            check(got[r0:r0 + n], x[r0:r0 + n], cols=L, scale=scale, row_offset=r0,
+                  what=f"C5 {kernel} rows {r0}+{n}")
+        del d_out
+        torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online"])
+def test_row_block_shards_equal_full_matrix(kernel):
+    # Row blocks launched with their absolute row offset reproduce the full
+    # matrix bit for bit (the multi-GPU sharding contract).
+    rows = cols = 4096
+    scale = float(np.float32(1 / np.sqrt(128)))
+    x = cs.generate(1, 0, batch=1, rows=rows, cols=cols)[0]
+    full = run(kernel, x, cols=cols, scale=scale)
+    for a, b in [(0, 1000), (1000, 2501), (2501, 4096)]:
+        part = run(kernel, x[a:b], cols=cols, scale=scale, row_offset=a)
+        assert np.array_equal(part, full[a:b]), (kernel, a, b)
+
+
+def test_deterministic_and_kernels_agree():
+    rows, cols = 777, 1500
+    x = cs.generate(2, 1, batch=1, rows=rows, cols=cols)[0]
+    outs = {}
+    for k in ("baseline", "tma", "pipeline", "online"):
+        a = run(k, x, cols=cols, scale=1.0)
+        assert np.array_equal(a, run(k, x, cols=cols, scale=1.0)), k
+        outs[k] = a
+    # Same causal math in every kernel: outputs within 1 FP16 ulp of each other.
+    base = outs["tma"].astype(np.int32)
+    for k, v in outs.items():
+        assert np.max(np.abs(v.astype(np.int32) - base)) <= 1, k
+    assert np.array_equal(outs["tma"], outs["pipeline"])
+
+
+@pytest.mark.parametrize("tuning", [(2, 2, 0), (2, 4, 1), (4, 3, 1), (8, 2, 0), (8, 3, 1)])
+def test_row_resident_tuning_variants(tuning):
+    for rows, cols in [(4096, 4096), (300, 2000), (1000, 40)]:
+        x = cs.generate(1, 0, batch=1, rows=rows, cols=cols)[0]
+        for kernel in ("tma", "pipeline"):
+            got = run(kernel, x, cols=cols, scale=0.125, tuning=tuning)
+            check(got, x, cols=cols, scale=0.125, what=f"{kernel} {tuning} {rows}x{cols}")
+
+
+def test_online_ring_depths_and_long_rows():
+    # Rows longer than half the ring take the two-fetch path.
+    for stages in (2, 3, 8, 16):
+        for rows, cols in [(40, 20000), (3, 70000), (600, 4100)]:
+            x = cs.generate(5, 4, batch=1, rows=rows, cols=cols)[0]
+            got = run("online", x, cols=cols, scale=0.0883883, tuning=(0, stages, -1))
+            check(got, x, cols=cols, scale=0.0883883, what=f"online S={stages} {rows}x{cols}")
+            # The same rows as the tail of a taller matrix (row offset).
+            got = run("online", x, cols=cols, scale=0.0883883, row_offset=5000, tuning=(0, stages, -1))
+            check(got, x, cols=cols, scale=0.0883883, row_offset=5000, what=f"online offset S={stages}")
+
+
+def test_batched_layout_with_gaps():
+    # batch_stride larger than rows * pitch (a view into a bigger buffer).
+    batch, rows, cols = 5, 100, 203
+    pitch = cs.padded_pitch(cols)
+    gap = 8 * 7
+    stride = rows * pitch + gap
+    flat = np.zeros(batch * stride, np.uint16)
+    x = cs.generate(2, 1, batch=batch, rows=rows, cols=cols)
+    for b in range(batch):
+        flat[b * stride:b * stride + rows * pitch] = x[b].ravel()
+    d_in = to_dev(flat)
+    d_out = sentinel_like(d_in)
+    for kernel in ("baseline", "tma", "pipeline", "online"):
+        d_out.view(torch.int16).fill_(int(np.uint16(SENTINEL).view(np.int16)))
+        with cs.Plan(d_in.data_ptr(), d_out.data_ptr(), rows=rows, cols=cols, pitch=pitch,
+                     batch=batch, batch_stride=stride) as plan:
+            plan.launch(kernel, 0.7)
+            assert plan.status() == (0, 0)
+        got = from_dev(d_out)
+        for b in range(batch):
+            blk = got[b * stride:b * stride + rows * pitch].reshape(rows, pitch)
+            check(blk, x[b], cols=cols, scale=0.7, what=f"gaps {kernel} {b}")
+            if b + 1 < batch:  # the gap between matrices is untouched
+                assert np.all(got[b * stride + rows * pitch:(b + 1) * stride] == SENTINEL)
+
+
+def test_one_shot_entry_points_match_plans():
+    rows, cols = 513, 700
+    pitch = cs.padded_pitch(cols)
+    x = cs.generate(1, 0, batch=2, rows=rows, cols=cols)
+    d_in = to_dev(x)
+    y = cs.softmax(d_in, cols=cols, scale=0.3)
+    torch.cuda.synchronize()
+    got = from_dev(y)
+    for b in range(2):
+        assert np.array_equal(got[b], run("auto", x[b], cols=cols, scale=0.3))
+    y1 = torch.empty_like(d_in[0])
+    rc = cs.lib().cs_softmax(cs.TMA, d_in[0].data_ptr(), y1.data_ptr(), rows, cols, pitch, 0.3,
+                             torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(from_dev(y1), got[0])
+
+
+def test_session_paths():
+    with cs.Session(0) as s:
+        s.probe()  # gpu/src/driver.rs:44-59
+        # prepare / launch / result with the sentinel and padding check.
+        rows, cols = 123, 77
+        dense = cs.make_input(rows, cols, "random", 0x13579BDF)
+        out = np.zeros_like(dense)
+        for kernel in ("baseline", "tma", "pipeline", "online"):
+            s.prepare(dense, rows, cols)
+            s.launch(kernel, 0.125)
+            s.result(out)
+            want = O.causal_softmax(dense, rows, cols, 0.125)[1]
+            name, acc = O.verify(out, want, rows, cols)
+            assert name == "ok", (kernel, name, acc.index)
+        # End to end from host buffers: equals the device path bit for bit.
+        batch, rows, cols = 7, 300, 301
+        xin = cs.generate(4, 3, batch=batch, rows=rows, cols=cols, pitch=cols)
+        hout = np.zeros_like(xin)
+        s.softmax_host(xin.ravel(), hout.reshape(-1), batch=batch, rows=rows, cols=cols, scale=0.2)
+        for b in (0, 3, 6):
+            dev = run("auto", O.pad(xin[b].ravel(), rows, cols).reshape(rows, -1), cols=cols, scale=0.2)
+            assert np.array_equal(O.unpad(dev.ravel(), rows, cols), hout[b].ravel())
+
+
+@pytest.mark.parametrize("kernel", ["tma", "pipeline", "online"])
+def test_bounded_wait_reports_timeout_and_context_survives(kernel):
+    # The producer issues no copies, so every consumer wait must run out after
+    # 1 ms; the kernel returns, the host reads CS_ERR_TIMEOUT, and the next
+    # normal launch on the same context is correct.
+    rows, cols = 64, 300
+    x = cs.generate(2, 1, batch=1, rows=rows, cols=cols)[0]
+    d_in = to_dev(x)
+    d_out = sentinel_like(d_in)
+    with cs.Plan.for_tensors(d_in, d_out, cols=cols) as plan:
+        plan.launch_debug(kernel, 1.0, cs.DEBUG_SKIP_LOADS, 1_000_000)
+        rc, status = plan.status()
+        assert rc == cs.ERR_CODE["TIMEOUT"] and status & cs.STATUS_TIMEOUT
+        plan.launch(kernel, 1.0)
+        assert plan.status() == (0, 0)
+    check(from_dev(d_out), x, cols=cols, scale=1.0, what=f"after timeout {kernel}")
+
+
+def test_argument_errors():
+    E = cs.ERR_CODE
+    x = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
+    y = torch.zeros_like(x)
+    L = cs.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.cs_softmax(cs.WARP, x.data_ptr(), y.data_ptr(), 64, 33, 64, 1.0, st) == E["WARP_COLS"]
+    assert L.cs_softmax(cs.TMA, x.data_ptr() + 2, y.data_ptr(), 8, 8, 8, 1.0, st) == E["ALIGNMENT"]
+    assert L.cs_softmax(cs.TMA, x.data_ptr(), x.data_ptr(), 8, 8, 8, 1.0, st) == E["ARG"]
+    assert L.cs_softmax(cs.TMA, x.data_ptr(), y.data_ptr(), 8, 8, 8, -1.0, st) == E["BAD_SCALE"]
+    assert L.cs_softmax(cs.TMA, x.data_ptr(), y.data_ptr(), 8, 9, 12, 1.0, st) == E["PITCH"]
+    assert L.cs_softmax(cs.TMA, None, y.data_ptr(), 8, 8, 8, 1.0, st) == E["NULL"]
+    assert L.cs_softmax(9, x.data_ptr(), y.data_ptr(), 8, 8, 8, 1.0, st) == E["BAD_KERNEL"]
+    assert L.cs_softmax(cs.TMA, x.data_ptr(), y.data_ptr(), 0, 8, 8, 1.0, st) == E["EMPTY"]
+    torch.cuda.synchronize()
