@@ -225,7 +225,11 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--tuning", default="", help="vec,stages,hint for the row-resident kernel")
+    ap.add_argument("--tuning", default="",
+                    help="vec,stages,l2_hint,zero_fill_tma for the row-resident kernel")
+    ap.add_argument("--matrices", type=int, default=MATRICES,
+                    help="heads in the batch (256 = the benchmark workload; smaller only for "
+                         "profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -256,9 +260,10 @@ def main() -> int:
     build.build_library()
     import causal_softmax as cs
 
-    if MATRICES % world:
-        raise SystemExit("256 heads must split evenly over the ranks")
-    n_local = MATRICES // world
+    n_total = args.matrices
+    if n_total % world:
+        raise SystemExit(f"{n_total} heads must split evenly over the ranks")
+    n_local = n_total // world
     first = rank * n_local
     scale = scale_f32()
 
@@ -274,8 +279,7 @@ def main() -> int:
     stream = torch.cuda.current_stream()
     plan = cs.Plan.for_tensors(d_in, d_out, cols=L)
     if args.tuning:
-        v, s_, h = (int(t) for t in args.tuning.split(","))
-        plan.set_tuning(v, s_, h)
+        plan.set_tuning(*(int(t) for t in args.tuning.split(",")))
     info = plan.describe(args.kernel)
     log(f"rank {rank}: launch {info}")
 
@@ -371,8 +375,9 @@ def main() -> int:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "io_dtype": "f16", "data": "synthetic",
-            "config": dict(WORKLOAD, kernel=info["kernel_name"], matrices_per_rank=n_local),
-            "matrices_per_s": round(MATRICES / (ms_step / 1e3), 2),
+            "config": dict(WORKLOAD, kernel=info["kernel_name"], matrices=n_total,
+                           matrices_per_rank=n_local),
+            "matrices_per_s": round(n_total / (ms_step / 1e3), 2),
             "roofline_pct": round(100.0 * value / (peak * world), 2),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": args.steps * world, "gpu_launches_per_rank": args.steps,

@@ -131,7 +131,7 @@ def _declare(L) -> None:
         "cs_plan_launch": (c_int, [vp, c_int, c_f32, vp]),
         "cs_plan_status": (c_int, [vp, ctypes.POINTER(ctypes.c_uint32)]),
         "cs_plan_set_timeout": (c_int, [vp, ctypes.c_uint64]),
-        "cs_plan_set_tuning": (c_int, [vp, c_int, c_int, c_int]),
+        "cs_plan_set_tuning": (c_int, [vp, c_int, c_int, c_int, c_int]),
         "cs_plan_describe": (c_int, [vp, c_int, ctypes.POINTER(LaunchInfo)]),
         "cs_plan_launch_debug": (c_int, [vp, c_int, c_f32, vp, ctypes.c_uint32, ctypes.c_uint64]),
         "cs_plan_destroy": (None, [vp]),
@@ -256,8 +256,10 @@ class Plan:
     def set_timeout(self, ns: int) -> None:
         check(lib().cs_plan_set_timeout(self._h, ns), "cs_plan_set_timeout")
 
-    def set_tuning(self, vec: int = 0, stages: int = 0, l2_hint: int = -1) -> None:
-        check(lib().cs_plan_set_tuning(self._h, vec, stages, l2_hint), "cs_plan_set_tuning")
+    def set_tuning(self, vec: int = 0, stages: int = 0, l2_hint: int = -1,
+                   zero_fill_tma: int = -1) -> None:
+        check(lib().cs_plan_set_tuning(self._h, vec, stages, l2_hint, zero_fill_tma),
+              "cs_plan_set_tuning")
 
     def describe(self, kernel="auto") -> dict:
         info = LaunchInfo()

@@ -80,21 +80,21 @@ void* rowres_fn() {
 
 // Maximum CTA size per vectors-per-thread choice (V) of the row-resident
 // kernel, which fixes its register budget: V = 2 runs with up to 1024
-// threads (64 registers), V = 4 with up to 768 (85), V = 8 with up to 576 (113).
-constexpr int rowres_maxt(int v) { return v == 8 ? 576 : (v == 4 ? 768 : 1024); }
+// threads (64 registers), V = 4 with up to 768 (80), V = 8 with up to 512 (128).
+constexpr int rowres_maxt(int v) { return v == 8 ? 512 : (v == 4 ? 768 : 1024); }
 
 void* rowres_kernel_ptr(int v, bool tma_store) {
   if (tma_store) {
     switch (v) {
       case 2: return rowres_fn<2, 1024, true>();
       case 4: return rowres_fn<4, 768, true>();
-      default: return rowres_fn<8, 576, true>();
+      default: return rowres_fn<8, 512, true>();
     }
   }
   switch (v) {
     case 2: return rowres_fn<2, 1024, false>();
     case 4: return rowres_fn<4, 768, false>();
-    default: return rowres_fn<8, 576, false>();
+    default: return rowres_fn<8, 512, false>();
   }
 }
 
@@ -168,9 +168,10 @@ int validate_args(int64_t batch, int64_t batch_stride, int64_t rows, int64_t col
 // ---------------------------------------------------------------------------
 
 struct Tuning {
-  int vec = 0;     // 0: automatic
-  int stages = 0;  // 0: automatic
-  int hint = -1;   // -1: automatic
+  int vec = 0;        // 0: automatic
+  int stages = 0;     // 0: automatic
+  int hint = -1;      // -1: automatic
+  int zero_tma = -1;  // -1: automatic
 };
 
 struct LaunchPlan {
@@ -192,21 +193,34 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
   return mx;
 }
 
+// Vectors per thread and CTA size for units of up to max_nv vectors: the
+// per-unit work (cursor, reductions, barriers) is paid by every thread, so
+// larger V (fewer threads per unit) wins once a CTA keeps >= 2 warps busy.
+bool rowres_shape(int64_t max_nv, int want_vec, int* vec, int* block) {
+  const int order[3] = {max_nv >= 8 * 64 ? 8 : (max_nv >= 4 * 64 ? 4 : 2), 4, 8};
+  for (int v : order) {
+    if (want_vec && v != want_vec) continue;
+    const int64_t thr = ((max_nv + v - 1) / v + 31) / 32 * 32;
+    if (thr <= rowres_maxt(v)) {
+      *vec = v;
+      *block = (int)std::max<int64_t>(thr, 32);
+      return true;
+    }
+  }
+  return false;
+}
+
 // Row-resident kernel geometry; CS_ERR_UNSUPPORTED when a unit does not fit.
 int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tma_store,
                 LaunchPlan* lp) {
-  const cs::UnitMap m = cs::make_unit_map(g);
-  const int64_t max_nv = rowres_max_vectors(g, m);
+  cs::UnitMap m = cs::make_unit_map(g, true);
+  int64_t max_nv = rowres_max_vectors(g, m);
   int vec = 0, block = 0;
-  const int choices[3] = {2, 4, 8};
-  for (int v : choices) {
-    if (t.vec && v != t.vec) continue;
-    const int64_t thr = ((max_nv + v - 1) / v + 31) / 32 * 32;
-    if (thr <= rowres_maxt(v)) {
-      vec = v;
-      block = (int)std::max<int64_t>(thr, 32);
-      break;
-    }
+  if (!rowres_shape(max_nv, t.vec, &vec, &block)) {
+    // A pair may not fit where a single row still does.
+    m = cs::make_unit_map(g, false);
+    max_nv = rowres_max_vectors(g, m);
+    rowres_shape(max_nv, t.vec, &vec, &block);
   }
   if (!vec) {
     std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: %lld vectors per unit do not fit",
@@ -244,6 +258,7 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
   lp->rr.stages = stages;
   lp->rr.stage_bytes = stage_bytes;
   lp->rr.l2_hint = t.hint < 0 ? 1 : t.hint;
+  lp->rr.zero_tma = t.zero_tma < 0 ? 1 : t.zero_tma;
   return CS_OK;
 }
 
@@ -335,8 +350,8 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
         if (ts) cs::rowres_kernel<4, 768, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
         else cs::rowres_kernel<4, 768, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
       } else {
-        if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        if (ts) cs::rowres_kernel<8, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<8, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
       }
       break;
     }
@@ -527,16 +542,21 @@ int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols) {
   if (kernel != CS_KERNEL_AUTO) return kernel;
   if (cols <= 32) return CS_KERNEL_WARP;
   // Host-side rule equal to make_plan's: the row-resident kernel takes any
-  // shape whose widest unit fits 576 threads x 8 vectors and two stages.
+  // shape whose widest unit (a row pair, else a single row) fits 512 threads
+  // x 8 vectors and two stages of shared memory.
   Geometry g{};
   g.batch = 1;
   g.rows = (int32_t)std::min<int64_t>(rows, kI32Max);
   g.cols = (int32_t)std::min<int64_t>(cols, kI32Max);
   g.pitch = (int32_t)std::min<int64_t>(padded_pitch(cols), kI32Max - 7);
-  const cs::UnitMap m = cs::make_unit_map(g);
-  const int64_t max_nv = rowres_max_vectors(g, m);
-  const int64_t stage = (max_nv * 16 + 127) / 128 * 128;
-  if (max_nv <= 8 * rowres_maxt(8) && 2 * stage + cs::rowres_tail_bytes(2) <= 232448) return CS_KERNEL_TMA;
+  for (bool paired : {true, false}) {
+    const cs::UnitMap m = cs::make_unit_map(g, paired);
+    const int64_t max_nv = rowres_max_vectors(g, m);
+    const int64_t stage = (max_nv * 16 + 127) / 128 * 128;
+    int vec = 0, block = 0;
+    if (rowres_shape(max_nv, 0, &vec, &block) && 2 * stage + cs::rowres_tail_bytes(2) <= 232448)
+      return CS_KERNEL_TMA;
+  }
   return CS_KERNEL_ONLINE;
 }
 
@@ -617,14 +637,16 @@ int cs_plan_set_timeout(cs_plan* plan, uint64_t timeout_ns) {
   return CS_OK;
 }
 
-int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint) {
+int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint, int zero_fill_tma) {
   if (!plan) return CS_ERR_NULL;
   if (vec_per_thread != 0 && vec_per_thread != 2 && vec_per_thread != 4 && vec_per_thread != 8)
     return CS_ERR_ARG;
   if (stages < 0 || stages > 24 || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
+  if (zero_fill_tma < -1 || zero_fill_tma > 1) return CS_ERR_ARG;
   plan->tuning.vec = vec_per_thread;
   plan->tuning.stages = stages;
   plan->tuning.hint = l2_hint;
+  plan->tuning.zero_tma = zero_fill_tma;
   return CS_OK;
 }
 

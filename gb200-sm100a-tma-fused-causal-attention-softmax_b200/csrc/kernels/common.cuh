@@ -65,18 +65,31 @@ __device__ __forceinline__ bool mbar_try_wait_parity(uint64_t* bar, uint32_t par
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `hint_ns` elapse, instead of re-issuing the probe.
+__device__ __forceinline__ bool mbar_try_wait_parity_sleep(uint64_t* bar, uint32_t parity,
+                                                           uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the phase with the given parity to complete, for at most
 // `timeout_ns` of GPU wall time. Returns false when the bound ran out.
-// try_wait itself suspends the thread for a hardware-chosen interval, so
-// this loop does not spin hot.
+// Each probe suspends the thread (hint 0.2 ms) until the phase completes,
+// so the loop neither spins hot nor steals issue slots from other warps.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint64_t timeout_ns) {
   if (mbar_try_wait_parity(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (mbar_try_wait_parity(bar, parity)) return true;
+    if (mbar_try_wait_parity_sleep(bar, parity, 200000u)) return true;
     if (global_timer_ns() - start > timeout_ns) return false;
   }
 }
@@ -125,6 +138,11 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Bound the number of bulk-store groups in flight (their source reads).
+__device__ __forceinline__ void bulk_wait_read_16() {
+  asm volatile("cp.async.bulk.wait_group.read 16;" ::: "memory");
+}
+
 // Wait until all committed bulk stores are complete (visible in global).
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -154,6 +172,38 @@ __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
 __device__ __forceinline__ uint32_t float2_to_half2_bits(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Packed-half helpers for the max pass (comparisons of halves are exact).
+constexpr uint32_t kHalfNegInf = 0xFC00u;
+
+// Replace halves at element index >= lim (0..7 within a 16-byte vector)
+// by -inf so they cannot win the row maximum.
+__device__ __forceinline__ uint4 mask_tail_neg_inf(uint4 r, int32_t lim) {
+  uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (2 * q >= lim) w[q] = (w[q] & 0xFFFF0000u) | kHalfNegInf;
+    if (2 * q + 1 >= lim) w[q] = (w[q] & 0x0000FFFFu) | (kHalfNegInf << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ __half2 bits_h2(uint32_t b) { return *reinterpret_cast<__half2*>(&b); }
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Maximum of the 8 halves of a vector, as a half.
+__device__ __forceinline__ __half max8_half(uint4 r) {
+  const __half2 m = __hmax2(__hmax2(bits_h2(r.x), bits_h2(r.y)), __hmax2(bits_h2(r.z), bits_h2(r.w)));
+  return __hmax(__low2half(m), __high2half(m));
+}
+
+// Butterfly max of a packed half pair across the warp.
+__device__ __forceinline__ uint32_t warp_max_h2(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    v = h2_bits(__hmax2(bits_h2(v), bits_h2(__shfl_xor_sync(0xffffffffu, v, o))));
+  return v;
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -44,11 +44,14 @@ __host__ __device__ __forceinline__ int32_t valid_cols(const Geometry& g, int32_
   return v < g.cols ? (int32_t)v : g.cols;
 }
 
-__host__ __device__ __forceinline__ UnitMap make_unit_map(const Geometry& g) {
+// paired == false makes every row its own unit (used when a pair would not
+// fit the kernel's registers but a single row does).
+__host__ __device__ __forceinline__ UnitMap make_unit_map(const Geometry& g, bool paired = true) {
   UnitMap m;
   int64_t tri = (int64_t)g.cols - 1 - g.row_offset;  // rows with valid < cols
   if (tri < 0) tri = 0;
   if (tri > g.rows) tri = g.rows;
+  if (!paired) tri = 0;
   m.n_tri = (int32_t)tri;
   m.n_pairs = m.n_tri / 2;
   m.units_per_matrix = m.n_pairs + (m.n_tri & 1) + (g.rows - m.n_tri);

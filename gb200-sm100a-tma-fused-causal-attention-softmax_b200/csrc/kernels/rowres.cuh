@@ -10,14 +10,19 @@
 //    shared-memory stages with 1-D TMA bulk copies (cp.async.bulk) completing
 //    on one mbarrier per stage; only round_up(valid, 8) elements are fetched,
 //    so the masked upper triangle is never read;
-//  * every thread moves its 16-byte vectors from the stage into registers
-//    (V vectors = 8V values per thread), and the stage is handed back to the
-//    producer after the first CTA barrier, so the next loads overlap compute;
+//  * every thread moves its V 16-byte vectors from the stage into registers;
+//    the stage goes back to the producer at the first CTA barrier, so the
+//    next copies overlap this unit's arithmetic;
+//  * the row maximum is taken on packed halves (exact), the logits are kept
+//    in base 2 (z = x * scale*log2(e), one rounding like the f32
+//    specification's x * scale), exp is computed once per element (MUFU ex2)
+//    and kept in registers, and the Blackwell packed-f32 instructions
+//    (mul/add .f32x2) halve the scaling, subtraction, summation and
+//    normalisation work; only a row's last vector needs masking;
 //  * max and sum are warp butterflies plus one cross-warp exchange each,
-//    for both rows of a pair at once (float2); exp is computed once per
-//    element (MUFU ex2) and kept in registers until the normalised FP16
-//    values are written with 16-byte stores;
-//  * the masked columns (and pitch padding) are written as 16-byte zero stores.
+//    for both rows of a pair at once;
+//  * the masked columns and pitch padding are written by TMA bulk stores
+//    from a zeroed shared-memory buffer (no loads, no per-thread stores).
 //
 // The `pipeline` kernel choice is the same kernel with kTmaStore: the
 // normalised FP16 row is written back into its stage and leaves through 1-D
@@ -34,17 +39,22 @@
 
 namespace cs {
 
+constexpr int kZeroBytes = 4096;  // zero source of the bulk zero-fill stores
+
 struct RowResParams {
   Geometry g;
   UnitMap m;
   int32_t stages;       // ring depth
   int32_t stage_bytes;  // bytes per stage (multiple of 128, >= 16 * max vectors per unit)
   int32_t l2_hint;      // 1: evict-first L2 hint on the input copies
+  int32_t zero_tma;     // 1: masked columns by bulk stores, 0: by thread stores
 };
 
-// Shared memory after the stages: 64 float2 reduction slots, one mbarrier per
-// stage and an abort flag.
-__host__ __device__ constexpr int rowres_tail_bytes(int stages) { return 64 * 8 + stages * 8 + 16; }
+// Shared memory after the stages: the zero buffer, 32 packed-half maxima,
+// 32 float2 sums, one mbarrier per stage and an abort flag.
+__host__ __device__ constexpr int rowres_tail_bytes(int stages) {
+  return kZeroBytes + 32 * 4 + 32 * 8 + stages * 8 + 16;
+}
 
 template <int V, int MAXT, bool kTmaStore>
 __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ RowResParams p) {
@@ -54,19 +64,36 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = T >> 5;
   const int S = p.stages;
   uint8_t* stage_base = smem;
-  float2* red = reinterpret_cast<float2*>(smem + (size_t)S * p.stage_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 64);
+  uint8_t* zero_buf = smem + (size_t)S * p.stage_bytes;
+  uint32_t* red_max = reinterpret_cast<uint32_t*>(zero_buf + kZeroBytes);
+  float2* red_sum = reinterpret_cast<float2*>(red_max + 32);
+  uint64_t* full = reinterpret_cast<uint64_t*>(red_sum + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + S);
 
   // Unit indices fit in 32 bits: the host splits launches so that
-  // total_units < 2^31.
+  // total_units < 2^30. Units advance by G per step; (matrix, unit) cursors
+  // are stepped incrementally instead of divided.
   const int32_t G = gridDim.x;
   const int32_t first = blockIdx.x;
   const int32_t total = (int32_t)p.m.total_units;
   const int32_t n_mine = first < total ? (total - 1 - first) / G + 1 : 0;
   const int32_t upm = p.m.units_per_matrix;
+  const int32_t gq = G / upm, gr = G - (G / upm) * upm;
+  auto advance = [&](int32_t& b, int32_t& k) {
+    k += gr;
+    b += gq;
+    if (k >= upm) {
+      k -= upm;
+      ++b;
+    }
+  };
+  int32_t cb = first / upm, ck = first - (first / upm) * upm;  // consumer cursor
+  int32_t pb = cb, pk = ck;                                    // producer cursor (thread 0)
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
 
+  for (int i = tid; i < kZeroBytes / 16; i += T)
+    reinterpret_cast<uint4*>(zero_buf)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();  // zero buffer visible to the bulk-store engine
   if (tid == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
     *abort_flag = 0;
@@ -74,18 +101,16 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
   }
   __syncthreads();
 
-  // Producer (thread 0): fetch the causal prefixes of local unit k into stage s.
+  // Producer (thread 0): fetch the causal prefixes of the next unit into stage s.
   uint64_t policy = 0;
   int32_t n_issued = 0;
-  auto issue = [&](int32_t k, int s) {
-    const int32_t u = first + k * G;
-    const int32_t b = u / upm;
+  auto issue_next = [&](int s) {
     int32_t ra, rb;
-    unit_rows(p.m, u - b * upm, ra, rb);
+    unit_rows(p.m, pk, ra, rb);
     const uint32_t va_vec = (uint32_t)(valid_cols(g, ra) + 7) >> 3;
     const uint32_t vb_vec = rb >= 0 ? (uint32_t)(valid_cols(g, rb) + 7) >> 3 : 0u;
     uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
-    const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
+    const uint16_t* src = g.in + (int64_t)pb * g.batch_stride;
     mbar_arrive_expect_tx(&full[s], (va_vec + vb_vec) * 16u);
     if (p.l2_hint) {
       bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, va_vec * 16u, &full[s], policy);
@@ -94,29 +119,41 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
       bulk_g2s(dst, src + (int64_t)ra * g.pitch, va_vec * 16u, &full[s]);
       if (vb_vec) bulk_g2s(dst + va_vec * 16u, src + (int64_t)rb * g.pitch, vb_vec * 16u, &full[s]);
     }
-    n_issued = k + 1;
+    advance(pb, pk);
+    ++n_issued;
+  };
+  // Zero columns [from_vec, pitch) of a row with bulk stores of the zero buffer.
+  const int32_t pv = g.pitch >> 3;  // 16-byte vectors per output row
+  auto zero_fill = [&](uint16_t* row, int32_t from_vec) {
+    uint8_t* dst = reinterpret_cast<uint8_t*>(row + (int64_t)from_vec * 8);
+    uint32_t left = (uint32_t)(pv - from_vec) * 16u;
+    while (left) {
+      const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
+      bulk_s2g(dst, zero_buf, n);
+      dst += n;
+      left -= n;
+    }
   };
 
   if (tid == 0 && !skip_loads) {
     if (p.l2_hint) policy = policy_evict_first();
     const int32_t pro = n_mine < S ? n_mine : S;
-    for (int32_t k = 0; k < pro; ++k) issue(k, k);
+    for (int32_t k = 0; k < pro; ++k) issue_next(k);
   }
 
-  const float scale = g.scale;
-  const int32_t pv = g.pitch >> 3;  // 16-byte vectors per output row
+  const float sl = g.scale * kLog2e;  // logits in base 2
+  const float2 sl2 = make_float2(sl, sl);
   int32_t k = 0;
-  int s = 0;             // k % S
-  uint32_t parity = 0;   // (k / S) & 1
+  int s = 0;            // k % S
+  uint32_t parity = 0;  // (k / S) & 1
   for (; k < n_mine; ++k, s = (s + 1 == S) ? 0 : s + 1, parity ^= (s == 0)) {
-    const int32_t u = first + k * G;
-    const int32_t b = u / upm;
     int32_t ra, rb;
-    unit_rows(p.m, u - b * upm, ra, rb);
+    unit_rows(p.m, ck, ra, rb);
     const int32_t va = valid_cols(g, ra);
     const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
     const int32_t na = (va + 7) >> 3;
-    const int32_t nv = na + ((vb + 7) >> 3);
+    const int32_t nb = (vb + 7) >> 3;
+    const int32_t nv = na + nb;
 
     const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
     if (!ok) {
@@ -125,89 +162,107 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     }
     const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
 
-    // Stage -> registers; scaled logits with masked slots at -inf.
-    float z[V][8];
-    float2 mx = make_float2(-INFINITY, -INFINITY);
+    // Stage -> registers; row maxima on packed halves (masked tail = -inf).
+    uint4 raw[V];
+    __half ma = __ushort_as_half((unsigned short)kHalfNegInf);
+    __half mb = ma;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       const int v = tid + j * T;
-      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-      if (ok && v < nv) raw = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
-      const bool in_a = v < na;
-      const int32_t lim = v < nv ? (in_a ? va - v * 8 : vb - (v - na) * 8) : 0;
-      const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
-      const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-      z[j][0] = f0.x * scale; z[j][1] = f0.y * scale;
-      z[j][2] = f1.x * scale; z[j][3] = f1.y * scale;
-      z[j][4] = f2.x * scale; z[j][5] = f2.y * scale;
-      z[j][6] = f3.x * scale; z[j][7] = f3.y * scale;
-      float vm = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (e >= lim) z[j][e] = -INFINITY;
-        vm = fmaxf(vm, z[j][e]);
+      raw[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (ok && v < nv) {
+        raw[j] = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
+        const bool in_a = v < na;
+        const int32_t lim = in_a ? va - v * 8 : vb - (v - na) * 8;
+        const __half mm = max8_half(lim < 8 ? mask_tail_neg_inf(raw[j], lim) : raw[j]);
+        if (in_a) ma = __hmax(ma, mm); else mb = __hmax(mb, mm);
       }
-      if (in_a) mx.x = fmaxf(mx.x, vm); else mx.y = fmaxf(mx.y, vm);
     }
-    mx = warp_max2(mx);
-    if (lane == 0) red[warp] = mx;
+    uint32_t mab = warp_max_h2(h2_bits(__halves2half2(ma, mb)));
+    if (lane == 0) red_max[warp] = mab;
     __syncthreads();  // stage s fully consumed; partial maxima published
     if (*abort_flag) break;
-    if (tid == 0 && !skip_loads) {
-      if (!kTmaStore) {
-        if (k + S < n_mine) issue(k + S, s);
-      } else if (k >= 1 && k - 1 + S < n_mine) {
-        bulk_wait_read_all();  // unit k-1's bulk store has left its stage
-        issue(k - 1 + S, s == 0 ? S - 1 : s - 1);
+
+    uint16_t* out_m = g.out + (int64_t)cb * g.batch_stride;
+    uint16_t* row_a = out_m + (int64_t)ra * g.pitch;
+    uint16_t* row_b = rb >= 0 ? out_m + (int64_t)rb * g.pitch : row_a;
+    if (tid == 0) {
+      if (!skip_loads) {
+        if (!kTmaStore) {
+          if (n_issued < n_mine) issue_next(s);
+        } else if (k >= 1 && n_issued < n_mine) {
+          bulk_wait_read_all();  // unit k-1's bulk store has left its stage
+          issue_next(s == 0 ? S - 1 : s - 1);
+        }
+      }
+      if (p.zero_tma) {
+        zero_fill(row_a, na);
+        if (rb >= 0) zero_fill(row_b, nb);
+        bulk_commit();
+        bulk_wait_read_16();
       }
     }
 
-    float2 t = lane < nwarps ? red[lane] : make_float2(-INFINITY, -INFINITY);
-    t = warp_max2(t);
+    mab = lane < nwarps ? red_max[lane] : (kHalfNegInf | (kHalfNegInf << 16));
+    mab = warp_max_h2(mab);
+    const float2 mf = __half22float2(bits_h2(mab));
+    const float m2a = mf.x * sl, m2b = mf.y * sl;  // = max of the rounded z = x*sl
 
-    float2 sm = make_float2(0.f, 0.f);
+    // exp2(z - max) once per element, kept in registers; partial sums.
+    float e[V][8];
+    float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       const int v = tid + j * T;
       if (v < nv) {
         const bool in_a = v < na;
-        const float m = in_a ? t.x : t.y;
-        float acc = 0.f;
+        const int32_t lim = in_a ? va - v * 8 : vb - (v - na) * 8;
+        const float nm = in_a ? -m2a : -m2b;
+        const float2 nm2 = make_float2(nm, nm);
+        const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          z[j][e] = ex2((z[j][e] - m) * kLog2e);  // masked: ex2(-inf) = +0
-          acc += z[j][e];
+        for (int q = 0; q < 4; ++q) {
+          const float2 d = __fadd2_rn(__fmul2_rn(__half22float2(bits_h2(w[q])), sl2), nm2);
+          e[j][2 * q] = ex2(d.x);
+          e[j][2 * q + 1] = ex2(d.y);
         }
-        if (in_a) sm.x += acc; else sm.y += acc;
+        if (lim < 8) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q >= lim) e[j][q] = 0.f;
+        }
+        const float2 acc = __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
+                                      __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7])));
+        if (in_a) sa = __fadd2_rn(sa, acc); else sb = __fadd2_rn(sb, acc);
       }
     }
-    sm = warp_sum2(sm);
-    if (lane == 0) red[32 + warp] = sm;
+    float2 sm = warp_sum2(make_float2(sa.x + sa.y, sb.x + sb.y));
+    if (lane == 0) red_sum[warp] = sm;
     __syncthreads();  // partial sums published
-    float2 q = lane < nwarps ? red[32 + lane] : make_float2(0.f, 0.f);
+    float2 q = lane < nwarps ? red_sum[lane] : make_float2(0.f, 0.f);
     q = warp_sum2(q);
     const float inv_a = rcp_rn(q.x);
     const float inv_b = rcp_rn(q.y);
 
-    uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
-    uint16_t* row_a = out_m + (int64_t)ra * g.pitch;
-    uint16_t* row_b = rb >= 0 ? out_m + (int64_t)rb * g.pitch : row_a;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       const int v = tid + j * T;
       if (v < nv) {
         const bool in_a = v < na;
         const float inv = in_a ? inv_a : inv_b;
-        uint4 o;
-        o.x = float2_to_half2_bits(z[j][0] * inv, z[j][1] * inv);
-        o.y = float2_to_half2_bits(z[j][2] * inv, z[j][3] * inv);
-        o.z = float2_to_half2_bits(z[j][4] * inv, z[j][5] * inv);
-        o.w = float2_to_half2_bits(z[j][6] * inv, z[j][7] * inv);
+        const float2 inv2 = make_float2(inv, inv);
+        uint32_t o[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 pr = __fmul2_rn(make_float2(e[j][2 * c], e[j][2 * c + 1]), inv2);
+          o[c] = float2_to_half2_bits(pr.x, pr.y);
+        }
+        const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
         if (kTmaStore) {
-          *reinterpret_cast<uint4*>(stage_base + (size_t)s * p.stage_bytes + (size_t)v * 16) = o;
+          *reinterpret_cast<uint4*>(stage_base + (size_t)s * p.stage_bytes + (size_t)v * 16) = ov;
         } else {
           uint16_t* dst = in_a ? row_a + (int64_t)v * 8 : row_b + (int64_t)(v - na) * 8;
-          *reinterpret_cast<uint4*>(dst) = o;
+          *reinterpret_cast<uint4*>(dst) = ov;
         }
       }
     }
@@ -217,21 +272,24 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
       if (tid == 0) {
         uint8_t* st_out = stage_base + (size_t)s * p.stage_bytes;
         bulk_s2g(row_a, st_out, (uint32_t)na * 16u);
-        if (rb >= 0) bulk_s2g(row_b, st_out + (size_t)na * 16, (uint32_t)(nv - na) * 16u);
+        if (rb >= 0) bulk_s2g(row_b, st_out + (size_t)na * 16, (uint32_t)nb * 16u);
         bulk_commit();
       }
     }
-    // Masked columns and pitch padding: 16-byte zero stores, no loads.
-    const int32_t za = pv - na;
-    const int32_t zb = rb >= 0 ? pv - ((vb + 7) >> 3) : 0;
-    const int32_t nb = (vb + 7) >> 3;
-    for (int32_t zi = tid; zi < za + zb; zi += T) {
-      uint16_t* dst = zi < za ? row_a + (int64_t)(na + zi) * 8 : row_b + (int64_t)(nb + zi - za) * 8;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if (!p.zero_tma) {
+      // Masked columns and pitch padding: 16-byte zero stores, no loads.
+      const int32_t za = pv - na;
+      const int32_t zb = rb >= 0 ? pv - nb : 0;
+      for (int32_t zi = tid; zi < za + zb; zi += T) {
+        uint16_t* dst = zi < za ? row_a + (int64_t)(na + zi) * 8 : row_b + (int64_t)(nb + zi - za) * 8;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
+    advance(cb, ck);
   }
 
-  if (kTmaStore && tid == 0) bulk_wait_all();  // stores must finish reading shared memory
+  // Bulk stores must finish reading shared memory before the CTA exits.
+  if ((kTmaStore || p.zero_tma) && tid == 0) bulk_wait_all();
 
   // After a timeout: let this CTA's own copies in flight land (bounded)
   // before the shared memory they target is released.

@@ -165,10 +165,12 @@ int cs_plan_status(cs_plan *plan, uint32_t *status);
  * launches of this plan (default 2 s). */
 int cs_plan_set_timeout(cs_plan *plan, uint64_t timeout_ns);
 
-/* Tuning knobs for the TMA / PIPELINE kernels (0 = automatic):
- * vectors per thread (2, 4 or 8), ring stages (1..16), L2 evict-first hint
- * on the input copies (0 off, 1 on, -1 automatic). */
-int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint);
+/* Tuning knobs (0 / -1 = automatic): vectors per thread of the TMA /
+ * PIPELINE kernels (2, 4 or 8), ring stages of the TMA / PIPELINE / ONLINE
+ * kernels (1..24), L2 evict-first hint on the input copies (0 off, 1 on),
+ * masked columns written by TMA bulk stores (1) or by thread stores (0). */
+int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint,
+                       int zero_fill_tma);
 
 typedef struct cs_launch_info {
     int32_t kernel;          /* resolved cs_kernel */

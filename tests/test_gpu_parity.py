@@ -200,16 +200,24 @@ def test_config5_long_context():
 
 
 @pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online"])
-def test_row_block_shards_equal_full_matrix(kernel):
+def test_row_block_shards_match_full_matrix(kernel):
     # Row blocks launched with their absolute row offset reproduce the full
-    # matrix bit for bit (the multi-GPU sharding contract).
+    # matrix (the multi-GPU sharding contract): each block passes the oracle
+    # check on its absolute rows, and agrees with the full launch within one
+    # FP16 ulp. Kernels whose per-row work split does not depend on the launch
+    # geometry (baseline, online) agree bit for bit; the row-resident kernel
+    # pairs rows per launch, which can move a row sum's last f32 bit.
     rows = cols = 4096
     scale = float(np.float32(1 / np.sqrt(128)))
     x = cs.generate(1, 0, batch=1, rows=rows, cols=cols)[0]
     full = run(kernel, x, cols=cols, scale=scale)
     for a, b in [(0, 1000), (1000, 2501), (2501, 4096)]:
         part = run(kernel, x[a:b], cols=cols, scale=scale, row_offset=a)
-        assert np.array_equal(part, full[a:b]), (kernel, a, b)
+        check(part, x[a:b], cols=cols, scale=scale, row_offset=a, what=f"{kernel} rows {a}:{b}")
+        diff = np.abs(part.astype(np.int32) - full[a:b].astype(np.int32))
+        assert diff.max() <= 1, (kernel, a, b)
+        if kernel in ("baseline", "online"):
+            assert diff.max() == 0, (kernel, a, b)
 
 
 def test_deterministic_and_kernels_agree():
@@ -227,7 +235,8 @@ def test_deterministic_and_kernels_agree():
     assert np.array_equal(outs["tma"], outs["pipeline"])
 
 
-@pytest.mark.parametrize("tuning", [(2, 2, 0), (2, 4, 1), (4, 3, 1), (8, 2, 0), (8, 3, 1)])
+@pytest.mark.parametrize("tuning", [(2, 2, 0, 0), (2, 4, 1, 1), (4, 3, 1, 0), (4, 2, 0, 1),
+                                    (8, 2, 0, 1), (8, 3, 1, 0), (8, 4, 1, 1)])
 def test_row_resident_tuning_variants(tuning):
     for rows, cols in [(4096, 4096), (300, 2000), (1000, 40)]:
         x = cs.generate(1, 0, batch=1, rows=rows, cols=cols)[0]
@@ -236,15 +245,33 @@ def test_row_resident_tuning_variants(tuning):
             check(got, x, cols=cols, scale=0.125, what=f"{kernel} {tuning} {rows}x{cols}")
 
 
+def test_unpaired_fallback_when_a_pair_does_not_fit():
+    # Forcing 2 vectors per thread caps a unit at 2048 vectors: row pairs of
+    # ~32000 columns do not fit, single rows do, so the planner drops pairing.
+    rows, cols, off = 40, 16384, 16000
+    x = cs.generate(5, 4, batch=1, rows=rows, cols=cols, first_row=off)[0]
+    d_in = to_dev(x)
+    d_out = sentinel_like(d_in)
+    with cs.Plan.for_tensors(d_in, d_out, cols=cols, row_offset=off) as plan:
+        plan.set_tuning(2, 0, -1, -1)
+        info = plan.describe("tma")
+        assert info["vec_per_thread"] == 2 and info["units"] == rows  # one unit per row
+        for kernel in ("tma", "pipeline"):
+            plan.launch(kernel, 0.0883883)
+            assert plan.status() == (0, 0)
+            check(from_dev(d_out), x, cols=cols, scale=0.0883883, row_offset=off, what=kernel)
+
+
 def test_online_ring_depths_and_long_rows():
     # Rows longer than half the ring take the two-fetch path.
     for stages in (2, 3, 8, 16):
         for rows, cols in [(40, 20000), (3, 70000), (600, 4100)]:
             x = cs.generate(5, 4, batch=1, rows=rows, cols=cols)[0]
-            got = run("online", x, cols=cols, scale=0.0883883, tuning=(0, stages, -1))
+            got = run("online", x, cols=cols, scale=0.0883883, tuning=(0, stages, -1, -1))
             check(got, x, cols=cols, scale=0.0883883, what=f"online S={stages} {rows}x{cols}")
             # The same rows as the tail of a taller matrix (row offset).
-            got = run("online", x, cols=cols, scale=0.0883883, row_offset=5000, tuning=(0, stages, -1))
+            got = run("online", x, cols=cols, scale=0.0883883, row_offset=5000,
+                      tuning=(0, stages, -1, -1))
             check(got, x, cols=cols, scale=0.0883883, row_offset=5000, what=f"online offset S={stages}")
 
 
