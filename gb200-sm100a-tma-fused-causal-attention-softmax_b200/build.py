@@ -25,8 +25,13 @@ LIB_PATH = os.path.join(LIB_DIR, "libcausal_softmax.so")
 CLI_PATH = os.path.join(BIN_DIR, "csm")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
-              "--expt-relaxed-constexpr"]
+# --fmad=false: no multiply-add contraction in device code. The kernels rely
+# on x*scale being rounded exactly once (so the row maximum's exponent is
+# exactly 0 after subtracting the rounded maximum), as the f32 specification
+# rounds it; a contracted x*scale - max would leave the product's rounding
+# residual, which at scale 1e30 is large enough to overflow exp.
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler",
+              "-fPIC,-ffp-contract=off", "--expt-relaxed-constexpr"]
 
 LIB_SOURCES = [os.path.join(CSRC, "api.cu"), os.path.join(CSRC, "host", "host.cpp")]
 CLI_SOURCES = [os.path.join(CSRC, "host", "cli.cpp")]

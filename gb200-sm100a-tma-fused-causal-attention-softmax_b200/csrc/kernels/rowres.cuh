@@ -206,7 +206,8 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     mab = lane < nwarps ? red_max[lane] : (kHalfNegInf | (kHalfNegInf << 16));
     mab = warp_max_h2(mab);
     const float2 mf = __half22float2(bits_h2(mab));
-    const float m2a = mf.x * sl, m2b = mf.y * sl;  // = max of the rounded z = x*sl
+    // Rounded exactly like the products below, so the maximum's exponent is 0.
+    const float m2a = __fmul_rn(mf.x, sl), m2b = __fmul_rn(mf.y, sl);
 
     // exp2(z - max) once per element, kept in registers; partial sums.
     float e[V][8];
