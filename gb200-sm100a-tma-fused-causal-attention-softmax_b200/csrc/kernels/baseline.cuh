@@ -19,16 +19,12 @@ struct BaselineParams {
   int64_t total_rows;
 };
 
-__device__ __forceinline__ void load_scaled8(const uint16_t* src, int32_t lim, float scale,
-                                             float z[8]) {
+__device__ __forceinline__ void load8(const uint16_t* src, float z[8]) {
   const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
   const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
   const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-  z[0] = f0.x * scale; z[1] = f0.y * scale; z[2] = f1.x * scale; z[3] = f1.y * scale;
-  z[4] = f2.x * scale; z[5] = f2.y * scale; z[6] = f3.x * scale; z[7] = f3.y * scale;
-#pragma unroll
-  for (int e = 0; e < 8; ++e)
-    if (e >= lim) z[e] = -INFINITY;
+  z[0] = f0.x; z[1] = f0.y; z[2] = f1.x; z[3] = f1.y;
+  z[4] = f2.x; z[5] = f2.y; z[6] = f3.x; z[7] = f3.y;
 }
 
 // Block-wide reduction of one float (max or sum); every thread gets the result.
@@ -48,7 +44,7 @@ __global__ void __launch_bounds__(256) baseline_kernel(const __grid_constant__ B
   __shared__ float red[32];
   const Geometry& g = p.g;
   const int32_t pv = g.pitch >> 3;
-  const float scale = g.scale;
+  const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   for (int64_t flat = blockIdx.x; flat < p.total_rows; flat += gridDim.x) {
     const int64_t b = flat / g.rows;
     const int32_t i = (int32_t)(flat - b * g.rows);
@@ -61,18 +57,21 @@ __global__ void __launch_bounds__(256) baseline_kernel(const __grid_constant__ B
     float m = -INFINITY;
     for (int32_t v = threadIdx.x; v < nvec; v += blockDim.x) {
       float z[8];
-      load_scaled8(src + (int64_t)v * 8, valid - v * 8, scale, z);
+      load8(src + (int64_t)v * 8, z);
+      const int32_t lim = valid - v * 8;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) m = fmaxf(m, z[e]);
+      for (int e = 0; e < 8; ++e)
+        if (e < lim) m = fmaxf(m, z[e]);
     }
     m = block_reduce<true>(m, red);
 
     float s = 0.f;
     for (int32_t v = threadIdx.x; v < nvec; v += blockDim.x) {
       float z[8];
-      load_scaled8(src + (int64_t)v * 8, valid - v * 8, scale, z);
+      load8(src + (int64_t)v * 8, z);
+      const int32_t lim = valid - v * 8;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s += ex2((z[e] - m) * kLog2e);
+      for (int e = 0; e < 8; ++e) s += e < lim ? ex2((z[e] - m) * sl) : 0.f;
     }
     s = block_reduce<false>(s, red);
     const float inv = rcp_rn(s);
@@ -81,9 +80,10 @@ __global__ void __launch_bounds__(256) baseline_kernel(const __grid_constant__ B
       uint4 o = make_uint4(0u, 0u, 0u, 0u);
       if (v < nvec) {
         float z[8];
-        load_scaled8(src + (int64_t)v * 8, valid - v * 8, scale, z);
+        load8(src + (int64_t)v * 8, z);
+        const int32_t lim = valid - v * 8;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) z[e] = ex2((z[e] - m) * kLog2e) * inv;
+        for (int e = 0; e < 8; ++e) z[e] = e < lim ? ex2((z[e] - m) * sl) * inv : 0.f;
         o.x = float2_to_half2_bits(z[0], z[1]);
         o.y = float2_to_half2_bits(z[2], z[3]);
         o.z = float2_to_half2_bits(z[4], z[5]);

@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(256) narrow_kernel(const __grid_constant__ Nar
   const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int32_t pv = g.pitch >> 3;
-  const float scale = g.scale;
+  const float sl = g.scale * kLog2e;
 
   for (int64_t base = warp_id * R; base < p.total_rows; base += n_warps * R) {
     const int64_t flat = base + lane / L;
@@ -47,21 +47,20 @@ __global__ void __launch_bounds__(256) narrow_kernel(const __grid_constant__ Nar
     {
       const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
       const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-      z[0] = f0.x * scale; z[1] = f0.y * scale; z[2] = f1.x * scale; z[3] = f1.y * scale;
-      z[4] = f2.x * scale; z[5] = f2.y * scale; z[6] = f3.x * scale; z[7] = f3.y * scale;
+      z[0] = f0.x; z[1] = f0.y; z[2] = f1.x; z[3] = f1.y;
+      z[4] = f2.x; z[5] = f2.y; z[6] = f3.x; z[7] = f3.y;
     }
     float m = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (e >= lim) z[e] = -INFINITY;
-      m = fmaxf(m, z[e]);
-    }
+    for (int e = 0; e < 8; ++e)
+      if (e < lim) m = fmaxf(m, z[e]);
 #pragma unroll
     for (int o = L / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // exp2((x - max) * scale*log2(e)): exactly 1 for the maximum at any scale.
     float s = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      z[e] = ex2((z[e] - m) * kLog2e);
+      z[e] = e < lim ? ex2((z[e] - m) * sl) : 0.f;
       s += z[e];
     }
 #pragma unroll

@@ -42,10 +42,11 @@ struct OnlineParams {
 __host__ __device__ constexpr int online_tail_bytes(int stages) { return 32 * 8 + stages * 8 + 16; }
 
 // (m, s) merge of two online-softmax partial states.
-__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+// m are row maxima of the raw values; sl = scale*log2(e).
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2, float sl) {
   const float mn = fmaxf(m, m2);
   if (mn == -INFINITY) return;  // both empty
-  s = s * ex2((m - mn) * kLog2e) + s2 * ex2((m2 - mn) * kLog2e);
+  s = s * ex2((m - mn) * sl) + s2 * ex2((m2 - mn) * sl);
   m = mn;
 }
 
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
   const int64_t n_rows = blockIdx.x < p.total_rows ? (p.total_rows - 1 - blockIdx.x) / G + 1 : 0;
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
   const int32_t pv = g.pitch >> 3;
-  const float scale = g.scale;
+  const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
@@ -160,20 +161,17 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
             const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * kOnlineTileBytes + (size_t)lv * 16);
             const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
             const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-            float z[8] = {f0.x * scale, f0.y * scale, f1.x * scale, f1.y * scale,
-                          f2.x * scale, f2.y * scale, f3.x * scale, f3.y * scale};
+            const float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
             const int32_t lim = valid - v * 8;
             float vm = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (e >= lim) z[e] = -INFINITY;
-              vm = fmaxf(vm, z[e]);
-            }
+            for (int e = 0; e < 8; ++e)
+              if (e < lim) vm = fmaxf(vm, z[e]);
             const float mn = fmaxf(m, vm);
             float acc = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc += ex2((z[e] - mn) * kLog2e);
-            s = (m == -INFINITY ? 0.f : s * ex2((m - mn) * kLog2e)) + acc;
+            for (int e = 0; e < 8; ++e) acc += e < lim ? ex2((z[e] - mn) * sl) : 0.f;
+            s = (m == -INFINITY ? 0.f : s * ex2((m - mn) * sl)) + acc;
             m = mn;
           }
         }
@@ -191,7 +189,7 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
       const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      online_merge(m, s, m2, s2);
+      online_merge(m, s, m2, s2, sl);
     }
     if (lane == 0) red[warp] = make_float2(m, s);
     __syncthreads();
@@ -202,7 +200,7 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, rm, o);
       const float s2 = __shfl_xor_sync(0xffffffffu, rs, o);
-      online_merge(rm, rs, m2, s2);
+      online_merge(rm, rs, m2, s2, sl);
     }
     const float inv = rcp_rn(rs);
     __syncthreads();  // red[] is rewritten by the next row
@@ -229,14 +227,10 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
             const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * kOnlineTileBytes + (size_t)lv * 16);
             const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
             const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-            float z[8] = {f0.x * scale, f0.y * scale, f1.x * scale, f1.y * scale,
-                          f2.x * scale, f2.y * scale, f3.x * scale, f3.y * scale};
+            float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
             const int32_t lim = valid - v * 8;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (e >= lim) z[e] = -INFINITY;
-              z[e] = ex2((z[e] - rm) * kLog2e) * inv;
-            }
+            for (int e = 0; e < 8; ++e) z[e] = e < lim ? ex2((z[e] - rm) * sl) * inv : 0.f;
             uint4 o;
             o.x = float2_to_half2_bits(z[0], z[1]);
             o.y = float2_to_half2_bits(z[2], z[3]);

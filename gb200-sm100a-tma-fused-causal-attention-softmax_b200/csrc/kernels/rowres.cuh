@@ -13,12 +13,12 @@
 //  * every thread moves its V 16-byte vectors from the stage into registers;
 //    the stage goes back to the producer at the first CTA barrier, so the
 //    next copies overlap this unit's arithmetic;
-//  * the row maximum is taken on packed halves (exact), the logits are kept
-//    in base 2 (z = x * scale*log2(e), one rounding like the f32
-//    specification's x * scale), exp is computed once per element (MUFU ex2)
-//    and kept in registers, and the Blackwell packed-f32 instructions
-//    (mul/add .f32x2) halve the scaling, subtraction, summation and
-//    normalisation work; only a row's last vector needs masking;
+//  * the row maximum is taken on packed halves (exact); each exponent is
+//    (x - max) * scale*log2(e) -- exactly 0 for the maximum and its ties --
+//    and exp is computed once per element (MUFU ex2) and kept in registers;
+//    the Blackwell packed-f32 instructions (add/mul .f32x2) halve the
+//    subtraction, scaling, summation and normalisation work; only a row's
+//    last vector needs masking;
 //  * max and sum are warp butterflies plus one cross-warp exchange each,
 //    for both rows of a pair at once;
 //  * the masked columns and pitch padding are written by TMA bulk stores
@@ -205,11 +205,12 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
 
     mab = lane < nwarps ? red_max[lane] : (kHalfNegInf | (kHalfNegInf << 16));
     mab = warp_max_h2(mab);
-    const float2 mf = __half22float2(bits_h2(mab));
-    // Rounded exactly like the products below, so the maximum's exponent is 0.
-    const float m2a = __fmul_rn(mf.x, sl), m2b = __fmul_rn(mf.y, sl);
+    const float2 mf = __half22float2(bits_h2(mab));  // row maxima of the halves
 
-    // exp2(z - max) once per element, kept in registers; partial sums.
+    // exp2((x - max) * scale*log2(e)) once per element, kept in registers.
+    // The difference comes first: it is 0 for the maximum (and for its ties)
+    // whatever the scale, and a product-then-subtract form would let the
+    // compiler fuse it into one FMA that keeps the product's rounding residual.
     float e[V][8];
     float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
 #pragma unroll
@@ -218,12 +219,12 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
       if (v < nv) {
         const bool in_a = v < na;
         const int32_t lim = in_a ? va - v * 8 : vb - (v - na) * 8;
-        const float nm = in_a ? -m2a : -m2b;
+        const float nm = in_a ? -mf.x : -mf.y;
         const float2 nm2 = make_float2(nm, nm);
         const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float2 d = __fadd2_rn(__fmul2_rn(__half22float2(bits_h2(w[q])), sl2), nm2);
+          const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w[q])), nm2), sl2);
           e[j][2 * q] = ex2(d.x);
           e[j][2 * q + 1] = ex2(d.y);
         }
