@@ -43,9 +43,16 @@ __host__ __device__ constexpr int online_tail_bytes(int stages) { return 32 * 8 
 
 // (m, s) merge of two online-softmax partial states.
 // m are row maxima of the raw values; sl = scale*log2(e).
+// An empty state has m == -inf; it is handled apart because (-inf - mn) * sl
+// is NaN when the scale is 0.
 __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2, float sl) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    s = s2;
+    return;
+  }
   const float mn = fmaxf(m, m2);
-  if (mn == -INFINITY) return;  // both empty
   s = s * ex2((m - mn) * sl) + s2 * ex2((m2 - mn) * sl);
   m = mn;
 }
