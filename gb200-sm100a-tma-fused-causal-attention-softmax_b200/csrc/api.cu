@@ -197,7 +197,8 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
 // per-unit work (cursor, reductions, barriers) is paid by every thread, so
 // larger V (fewer threads per unit) wins once a CTA keeps >= 2 warps busy.
 bool rowres_shape(int64_t max_nv, int want_vec, int* vec, int* block) {
-  const int order[3] = {max_nv >= 8 * 64 ? 8 : (max_nv >= 4 * 64 ? 4 : 2), 4, 8};
+  const int pref = max_nv >= 8 * 64 ? 8 : (max_nv >= 4 * 64 ? 4 : 2);
+  const int order[4] = {pref, 4, 8, 2};
   for (int v : order) {
     if (want_vec && v != want_vec) continue;
     const int64_t thr = ((max_nv + v - 1) / v + 31) / 32 * 32;
