@@ -140,7 +140,8 @@ def _declare(L) -> None:
                                        c_f32, vp]),
         "cs_session_create": (c_int, [ctypes.POINTER(vp), c_int]),
         "cs_session_probe": (c_int, [vp]),
-        "cs_session_softmax_host": (c_int, [vp, c_int, u16p, u16p, c_i64, c_i32, c_i32, c_f32]),
+        "cs_session_softmax_host": (c_int, [vp, c_int, u16p, u16p, c_i64, c_i32, c_i32, c_i32,
+                                            c_f32]),
         "cs_session_prepare": (c_int, [vp, u16p, c_i32, c_i32]),
         "cs_session_launch": (c_int, [vp, c_int, c_f32]),
         "cs_session_result": (c_int, [vp, u16p]),
@@ -297,10 +298,11 @@ class Session:
         check(lib().cs_session_probe(self._h), "cs_session_probe")
 
     def softmax_host(self, h_in, h_out, *, batch: int, rows: int, cols: int, scale: float,
-                     kernel="auto") -> None:
+                     kernel="auto", row_offset: int = 0) -> None:
         """h_in/h_out: numpy uint16 arrays of batch*rows*cols dense halves (pinned for speed)."""
         check(lib().cs_session_softmax_host(self._h, kernel_id(kernel), _u16p(h_in), _u16p(h_out),
-                                            batch, rows, cols, scale), "cs_session_softmax_host")
+                                            batch, rows, cols, row_offset, scale),
+              "cs_session_softmax_host")
 
     def prepare(self, h_in, rows: int, cols: int) -> None:
         check(lib().cs_session_prepare(self._h, _u16p(h_in), rows, cols), "cs_session_prepare")

@@ -808,10 +808,11 @@ static int session_read_status(cs_session* s) {
 }
 
 int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
-                            int64_t batch, int32_t rows, int32_t cols, float scale) {
+                            int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
+                            float scale) {
   if (!session || !h_in || !h_out) return CS_ERR_NULL;
   const int64_t pitch = padded_pitch(cols);
-  int rc = validate_args(batch, (int64_t)rows * pitch, rows, cols, pitch, 0, scale);
+  int rc = validate_args(batch, (int64_t)rows * pitch, rows, cols, pitch, row_offset, scale);
   if (rc) return rc;
   if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
   DeviceGuard guard(session->device);
@@ -853,7 +854,7 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     g.rows = rows;
     g.cols = cols;
     g.pitch = (int32_t)pitch;
-    g.row_offset = 0;
+    g.row_offset = row_offset;
     g.scale = scale;
     g.status = session->d_status;
     g.timeout_ns = kDefaultTimeoutNs;

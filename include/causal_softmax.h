@@ -224,14 +224,15 @@ int cs_session_probe(cs_session *session);
 
 /* End to end from host memory: `batch` dense rows x cols matrices (no
  * padding, like reference/src/lib.rs:85) are copied to the device with the
- * padded pitch, softmaxed, and copied back unpadded into h_out. Chunks of
+ * padded pitch, softmaxed, and copied back unpadded into h_out. Local row i
+ * is absolute causal row row_offset + i (0 for whole matrices). Chunks of
  * matrices alternate between two streams so host->device copies, kernels and
  * device->host copies overlap; device buffers are cached in the session.
  * Pinned host memory (cs_host_register) makes the copies asynchronous.
  * Returns after the last copy has landed; checks the status word. */
 int cs_session_softmax_host(cs_session *session, int kernel, const uint16_t *h_in,
                             uint16_t *h_out, int64_t batch, int32_t rows, int32_t cols,
-                            float scale);
+                            int32_t row_offset, float scale);
 
 /* The reference's prepare / launch / result cycle (gpu/src/driver.rs:65-95,
  * 108-211, 213-232) for one matrix: prepare copies `h_in` (dense rows x cols)
