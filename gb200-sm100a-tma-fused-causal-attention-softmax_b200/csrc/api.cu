@@ -78,23 +78,24 @@ void* rowres_fn() {
   return reinterpret_cast<void*>(&cs::rowres_kernel<V, MAXT, TS>);
 }
 
-// Maximum CTA size per vectors-per-thread choice (V) of the row-resident
-// kernel, which fixes its register budget: V = 2 runs with up to 1024
-// threads (64 registers), V = 4 with up to 768 (80), V = 8 with up to 512 (128).
-constexpr int rowres_maxt(int v) { return v == 8 ? 512 : (v == 4 ? 768 : 1024); }
+// Maximum CTA size (consumer warps + the producer warp) per vectors-per-thread
+// choice V of the row-resident kernel, which fixes its register budget:
+// V = 2 up to 1024 threads (64 registers), V = 4 up to 512 (128), V = 8 up
+// to 576 (96; long single rows of up to 32768 columns).
+constexpr int rowres_maxt(int v) { return v == 8 ? 576 : (v == 4 ? 512 : 1024); }
 
 void* rowres_kernel_ptr(int v, bool tma_store) {
   if (tma_store) {
     switch (v) {
       case 2: return rowres_fn<2, 1024, true>();
-      case 4: return rowres_fn<4, 768, true>();
-      default: return rowres_fn<8, 512, true>();
+      case 4: return rowres_fn<4, 512, true>();
+      default: return rowres_fn<8, 576, true>();
     }
   }
   switch (v) {
     case 2: return rowres_fn<2, 1024, false>();
-    case 4: return rowres_fn<4, 768, false>();
-    default: return rowres_fn<8, 512, false>();
+    case 4: return rowres_fn<4, 512, false>();
+    default: return rowres_fn<8, 576, false>();
   }
 }
 
@@ -193,18 +194,17 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
   return mx;
 }
 
-// Vectors per thread and CTA size for units of up to max_nv vectors: the
-// per-unit work (cursor, reductions, barriers) is paid by every thread, so
-// larger V (fewer threads per unit) wins once a CTA keeps >= 2 warps busy.
-bool rowres_shape(int64_t max_nv, int want_vec, int* vec, int* block) {
-  const int pref = max_nv >= 8 * 64 ? 8 : (max_nv >= 4 * 64 ? 4 : 2);
-  const int order[4] = {pref, 4, 8, 2};
+// Vectors per thread and CTA size for units of up to max_nv vectors. Each
+// consumer warp owns 32*V vectors of one row; a row pair needs one warp more
+// than its total in the worst split. One producer warp is added.
+bool rowres_shape(int64_t max_nv, bool paired, int want_vec, int* vec, int* block) {
+  const int order[3] = {4, 8, 2};
   for (int v : order) {
     if (want_vec && v != want_vec) continue;
-    const int64_t thr = ((max_nv + v - 1) / v + 31) / 32 * 32;
-    if (thr <= rowres_maxt(v)) {
+    const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
+    if (warps <= 31 && 32 * warps <= rowres_maxt(v)) {
       *vec = v;
-      *block = (int)std::max<int64_t>(thr, 32);
+      *block = (int)(32 * warps);
       return true;
     }
   }
@@ -217,11 +217,11 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
   cs::UnitMap m = cs::make_unit_map(g, true);
   int64_t max_nv = rowres_max_vectors(g, m);
   int vec = 0, block = 0;
-  if (!rowres_shape(max_nv, t.vec, &vec, &block)) {
+  if (!rowres_shape(max_nv, m.n_pairs > 0, t.vec, &vec, &block)) {
     // A pair may not fit where a single row still does.
     m = cs::make_unit_map(g, false);
     max_nv = rowres_max_vectors(g, m);
-    rowres_shape(max_nv, t.vec, &vec, &block);
+    rowres_shape(max_nv, false, t.vec, &vec, &block);
   }
   if (!vec) {
     std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: %lld vectors per unit do not fit",
@@ -348,11 +348,11 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
         if (ts) cs::rowres_kernel<2, 1024, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
         else cs::rowres_kernel<2, 1024, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
       } else if (lp.vec == 4) {
-        if (ts) cs::rowres_kernel<4, 768, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<4, 768, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        if (ts) cs::rowres_kernel<4, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<4, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
       } else {
-        if (ts) cs::rowres_kernel<8, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<8, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+        else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
       }
       break;
     }
@@ -555,7 +555,8 @@ int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols) {
     const int64_t max_nv = rowres_max_vectors(g, m);
     const int64_t stage = (max_nv * 16 + 127) / 128 * 128;
     int vec = 0, block = 0;
-    if (rowres_shape(max_nv, 0, &vec, &block) && 2 * stage + cs::rowres_tail_bytes(2) <= 232448)
+    if (rowres_shape(max_nv, m.n_pairs > 0, 0, &vec, &block) &&
+        2 * stage + cs::rowres_tail_bytes(2) <= 232448)
       return CS_KERNEL_TMA;
   }
   return CS_KERNEL_ONLINE;

@@ -6,28 +6,26 @@
 //  * persistent grid (SM count x resident CTAs); CTA c takes work units
 //    c, c+G, c+2G, ... of the pair map in geometry.cuh, so every unit carries
 //    the same number of causal elements and the schedule is balanced statically;
-//  * one elected thread streams each unit's row prefixes into a ring of
-//    shared-memory stages with 1-D TMA bulk copies (cp.async.bulk) completing
-//    on one mbarrier per stage; only round_up(valid, 8) elements are fetched,
-//    so the masked upper triangle is never read;
-//  * every thread moves its V 16-byte vectors from the stage into registers;
-//    the stage goes back to the producer at the first CTA barrier, so the
-//    next copies overlap this unit's arithmetic;
-//  * the row maximum is taken on packed halves (exact); each exponent is
-//    (x - max) * scale*log2(e) -- exactly 0 for the maximum and its ties --
-//    and exp is computed once per element (MUFU ex2) and kept in registers;
-//    the Blackwell packed-f32 instructions (add/mul .f32x2) halve the
-//    subtraction, scaling, summation and normalisation work; only a row's
-//    last vector needs masking;
-//  * max and sum are warp butterflies plus one cross-warp exchange each,
-//    for both rows of a pair at once;
-//  * the masked columns and pitch padding are written by TMA bulk stores
-//    from a zeroed shared-memory buffer (no loads, no per-thread stores).
+//  * warp-specialised: one producer warp streams each unit's row prefixes
+//    into a ring of shared-memory stages with 1-D TMA bulk copies
+//    (cp.async.bulk, completing on a `full` mbarrier per stage) and writes the
+//    masked columns and pitch padding with TMA bulk stores from a zeroed
+//    shared buffer; only round_up(valid, 8) elements are ever read;
+//  * consumer warps each own a contiguous segment of ONE row (32*V 16-byte
+//    vectors, lane-interleaved so every load/store instruction of a warp
+//    covers 512 contiguous bytes); a warp releases its stage (`empty`
+//    mbarrier) as soon as its vectors are in registers;
+//  * each warp reduces its own (max, sum) with shuffle butterflies -- the max
+//    on packed halves (exact), the exponents as (x - max) * scale*log2(e)
+//    with the Blackwell packed f32x2 add/mul, exp computed once per element
+//    with MUFU ex2 and kept in registers -- and publishes it; after ONE
+//    named barrier per unit the warps of a row merge the partials (online
+//    softmax rescaling) and write p = e * 2^((m_w - M)*scale*log2 e) / S;
+//  * partials are double-buffered, so that one barrier suffices.
 //
-// The `pipeline` kernel choice is the same kernel with kTmaStore: the
-// normalised FP16 row is written back into its stage and leaves through 1-D
-// TMA bulk stores (cp.async.bulk shared->global), and a stage is refilled
-// one unit later, once its bulk store has finished reading it.
+// The `pipeline` kernel choice is the same kernel with kTmaStore: consumers
+// write the normalised FP16 row back into the stage, and the producer warp
+// sends it with TMA bulk stores (shared->global) before refilling the stage.
 //
 // Every mbarrier wait is bounded (Geometry::timeout_ns); on expiry the kernel
 // sets kStatusTimeout in the status word, waits (bounded) for its own copies
@@ -47,257 +45,288 @@ struct RowResParams {
   int32_t stages;       // ring depth
   int32_t stage_bytes;  // bytes per stage (multiple of 128, >= 16 * max vectors per unit)
   int32_t l2_hint;      // 1: evict-first L2 hint on the input copies
-  int32_t zero_tma;     // 1: masked columns by bulk stores, 0: by thread stores
+  int32_t zero_tma;     // 1: masked columns by bulk stores, 0: by consumer stores
 };
 
-// Shared memory after the stages: the zero buffer, 32 packed-half maxima,
-// 32 float2 sums, one mbarrier per stage and an abort flag.
+// Shared memory after the stages: zero buffer, 2 x 32 float2 (max, sum)
+// partials, full and empty mbarriers per stage, abort flag.
 __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
-  return kZeroBytes + 32 * 4 + 32 * 8 + stages * 8 + 16;
+  return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
+}
+
+// Online-softmax merge of (m2, s2) into (m, s); empty states have m = -inf.
+__device__ __forceinline__ void merge_ms(float& m, float& s, float m2, float s2, float sl) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    s = s2;
+    return;
+  }
+  const float mn = fmaxf(m, m2);
+  s = s * ex2((m - mn) * sl) + s2 * ex2((m2 - mn) * sl);
+  m = mn;
 }
 
 template <int V, int MAXT, bool kTmaStore>
 __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ RowResParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Geometry& g = p.g;
-  const int T = blockDim.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = T >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int W = (blockDim.x >> 5) - 1;  // consumer warps; warp W is the producer
   const int S = p.stages;
   uint8_t* stage_base = smem;
   uint8_t* zero_buf = smem + (size_t)S * p.stage_bytes;
-  uint32_t* red_max = reinterpret_cast<uint32_t*>(zero_buf + kZeroBytes);
-  float2* red_sum = reinterpret_cast<float2*>(red_max + 32);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red_sum + 32);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + S);
+  float2* red = reinterpret_cast<float2*>(zero_buf + kZeroBytes);  // [2][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 64);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
-  // Unit indices fit in 32 bits: the host splits launches so that
-  // total_units < 2^30. Units advance by G per step; (matrix, unit) cursors
-  // are stepped incrementally instead of divided.
+  // Units advance by G per step; (matrix, unit) cursors are stepped
+  // incrementally. The host splits launches so that total_units < 2^30.
   const int32_t G = gridDim.x;
   const int32_t first = blockIdx.x;
   const int32_t total = (int32_t)p.m.total_units;
   const int32_t n_mine = first < total ? (total - 1 - first) / G + 1 : 0;
   const int32_t upm = p.m.units_per_matrix;
   const int32_t gq = G / upm, gr = G - (G / upm) * upm;
-  auto advance = [&](int32_t& b, int32_t& k) {
-    k += gr;
-    b += gq;
-    if (k >= upm) {
-      k -= upm;
-      ++b;
-    }
-  };
-  int32_t cb = first / upm, ck = first - (first / upm) * upm;  // consumer cursor
-  int32_t pb = cb, pk = ck;                                    // producer cursor (thread 0)
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
+  const int32_t pv = g.pitch >> 3;  // 16-byte vectors per output row
 
-  for (int i = tid; i < kZeroBytes / 16; i += T)
+  for (int i = tid; i < kZeroBytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(zero_buf)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async_smem();  // zero buffer visible to the bulk-store engine
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)W);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
-  // Producer (thread 0): fetch the causal prefixes of the next unit into stage s.
-  uint64_t policy = 0;
-  int32_t n_issued = 0;
-  auto issue_next = [&](int s) {
-    int32_t ra, rb;
-    unit_rows(p.m, pk, ra, rb);
-    const uint32_t va_vec = (uint32_t)(valid_cols(g, ra) + 7) >> 3;
-    const uint32_t vb_vec = rb >= 0 ? (uint32_t)(valid_cols(g, rb) + 7) >> 3 : 0u;
-    uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
-    const uint16_t* src = g.in + (int64_t)pb * g.batch_stride;
-    mbar_arrive_expect_tx(&full[s], (va_vec + vb_vec) * 16u);
-    if (p.l2_hint) {
-      bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, va_vec * 16u, &full[s], policy);
-      if (vb_vec) bulk_g2s_hint(dst + va_vec * 16u, src + (int64_t)rb * g.pitch, vb_vec * 16u, &full[s], policy);
-    } else {
-      bulk_g2s(dst, src + (int64_t)ra * g.pitch, va_vec * 16u, &full[s]);
-      if (vb_vec) bulk_g2s(dst + va_vec * 16u, src + (int64_t)rb * g.pitch, vb_vec * 16u, &full[s]);
+  if (warp == W) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0 || skip_loads) return;
+    const uint64_t policy = p.l2_hint ? policy_evict_first() : 0ull;
+    int32_t b = first / upm, kk = first - (first / upm) * upm;  // unit cursor
+    // kTmaStore: the output of the unit that last used a stage is stored
+    // from it before the stage is refilled.
+    auto store_unit = [&](int32_t ub, int32_t uk, int s) {
+      int32_t ra, rb;
+      unit_rows(p.m, uk, ra, rb);
+      const uint32_t na = (uint32_t)(valid_cols(g, ra) + 7) >> 3;
+      const uint32_t nb = rb >= 0 ? (uint32_t)(valid_cols(g, rb) + 7) >> 3 : 0u;
+      uint16_t* out_m = g.out + (int64_t)ub * g.batch_stride;
+      const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
+      bulk_s2g(out_m + (int64_t)ra * g.pitch, st, na * 16u);
+      if (nb) bulk_s2g(out_m + (int64_t)rb * g.pitch, st + (size_t)na * 16, nb * 16u);
+      bulk_commit();
+    };
+    int32_t sb[24], sk[24];  // unit held by each stage (kTmaStore)
+    bool aborted = false;
+    int32_t issued = 0;
+    for (int32_t k = 0; k < n_mine; ++k) {
+      const int s = k % S;
+      if (k >= S) {
+        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
+          aborted = true;
+          break;
+        }
+        if (kTmaStore) {
+          store_unit(sb[s], sk[s], s);
+          bulk_wait_read_all();  // the stage is read out before it is refilled
+        }
+      }
+      int32_t ra, rb;
+      unit_rows(p.m, kk, ra, rb);
+      const int32_t va = valid_cols(g, ra);
+      const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
+      const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
+      uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+      const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
+      mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
+      if (p.l2_hint) {
+        bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
+        if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
+      } else {
+        bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
+        if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
+      }
+      ++issued;
+      if (p.zero_tma) {
+        uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
+        for (int r = 0; r < 2; ++r) {
+          const int32_t row = r == 0 ? ra : rb;
+          if (row < 0) break;
+          uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
+          uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
+          while (left) {
+            const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
+            bulk_s2g(z, zero_buf, n);
+            z += n;
+            left -= n;
+          }
+        }
+        bulk_commit();
+        bulk_wait_read_16();
+      }
+      if (kTmaStore) {
+        sb[s] = b;
+        sk[s] = kk;
+      }
+      kk += gr;
+      b += gq;
+      if (kk >= upm) {
+        kk -= upm;
+        ++b;
+      }
     }
-    advance(pb, pk);
-    ++n_issued;
-  };
-  // Zero columns [from_vec, pitch) of a row with bulk stores of the zero buffer.
-  const int32_t pv = g.pitch >> 3;  // 16-byte vectors per output row
-  auto zero_fill = [&](uint16_t* row, int32_t from_vec) {
-    uint8_t* dst = reinterpret_cast<uint8_t*>(row + (int64_t)from_vec * 8);
-    uint32_t left = (uint32_t)(pv - from_vec) * 16u;
-    while (left) {
-      const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
-      bulk_s2g(dst, zero_buf, n);
-      dst += n;
-      left -= n;
+    if (kTmaStore && !aborted) {
+      // Outputs of the last min(S, n_mine) units.
+      for (int32_t k = n_mine; k < n_mine + S && k - S < n_mine; ++k) {
+        if (k < S) continue;
+        const int s = k % S;
+        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) break;
+        store_unit(sb[s], sk[s], s);
+      }
     }
-  };
-
-  if (tid == 0 && !skip_loads) {
-    if (p.l2_hint) policy = policy_evict_first();
-    const int32_t pro = n_mine < S ? n_mine : S;
-    for (int32_t k = 0; k < pro; ++k) issue_next(k);
+    bulk_wait_all();
+    // Copies this warp issued that no consumer waited for (after an abort).
+    for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
+      (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+    return;
   }
 
-  const float sl = g.scale * kLog2e;  // logits in base 2
+  // -------------------------------------------------------------- consumers
+  const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   const float2 sl2 = make_float2(sl, sl);
-  int32_t k = 0;
-  int s = 0;            // k % S
-  uint32_t parity = 0;  // (k / S) & 1
-  for (; k < n_mine; ++k, s = (s + 1 == S) ? 0 : s + 1, parity ^= (s == 0)) {
+  constexpr int kSeg = 32 * V;  // vectors per warp segment
+  int32_t b = first / upm, kk = first - (first / upm) * upm;
+  int s = 0;
+  uint32_t parity = 0;
+  for (int32_t k = 0; k < n_mine; ++k) {
     int32_t ra, rb;
-    unit_rows(p.m, ck, ra, rb);
+    unit_rows(p.m, kk, ra, rb);
     const int32_t va = valid_cols(g, ra);
     const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
-    const int32_t na = (va + 7) >> 3;
-    const int32_t nb = (vb + 7) >> 3;
-    const int32_t nv = na + nb;
+    const int32_t na = (va + 7) >> 3, nb = (vb + 7) >> 3;
+    const int32_t wa = (na + kSeg - 1) / kSeg, wb = (nb + kSeg - 1) / kSeg;
+    // This warp's row and segment (warps past wa + wb sit this unit out).
+    const bool row_a = warp < wa;
+    const bool active = warp < wa + wb;
+    const int32_t seg = row_a ? warp : warp - wa;
+    const int32_t n_row = row_a ? na : nb;
+    const int32_t valid = row_a ? va : vb;
+    const int32_t v0 = seg * kSeg + lane;  // this lane's first vector within the row
 
     const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
     if (!ok) {
       *abort_flag = 1;
       if (g.status) atomicOr(g.status, kStatusTimeout);
     }
-    const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
+    const uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
 
-    // Stage -> registers; row maxima on packed halves (masked tail = -inf).
     uint4 raw[V];
-    __half ma = __ushort_as_half((unsigned short)kHalfNegInf);
-    __half mb = ma;
+    __half hm = __ushort_as_half((unsigned short)kHalfNegInf);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int v = tid + j * T;
+      const int32_t v = v0 + 32 * j;
       raw[j] = make_uint4(0u, 0u, 0u, 0u);
-      if (ok && v < nv) {
+      if (ok && active && v < n_row) {
         raw[j] = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
-        const bool in_a = v < na;
-        const int32_t lim = in_a ? va - v * 8 : vb - (v - na) * 8;
-        const __half mm = max8_half(lim < 8 ? mask_tail_neg_inf(raw[j], lim) : raw[j]);
-        if (in_a) ma = __hmax(ma, mm); else mb = __hmax(mb, mm);
+        const int32_t lim = valid - v * 8;
+        hm = __hmax(hm, max8_half(lim < 8 ? mask_tail_neg_inf(raw[j], lim) : raw[j]));
       }
     }
-    uint32_t mab = warp_max_h2(h2_bits(__halves2half2(ma, mb)));
-    if (lane == 0) red_max[warp] = mab;
-    __syncthreads();  // stage s fully consumed; partial maxima published
-    if (*abort_flag) break;
-
-    uint16_t* out_m = g.out + (int64_t)cb * g.batch_stride;
-    uint16_t* row_a = out_m + (int64_t)ra * g.pitch;
-    uint16_t* row_b = rb >= 0 ? out_m + (int64_t)rb * g.pitch : row_a;
-    if (tid == 0) {
-      if (!skip_loads) {
-        if (!kTmaStore) {
-          if (n_issued < n_mine) issue_next(s);
-        } else if (k >= 1 && n_issued < n_mine) {
-          bulk_wait_read_all();  // unit k-1's bulk store has left its stage
-          issue_next(s == 0 ? S - 1 : s - 1);
-        }
-      }
-      if (p.zero_tma) {
-        zero_fill(row_a, na);
-        if (rb >= 0) zero_fill(row_b, nb);
-        bulk_commit();
-        bulk_wait_read_16();
-      }
+    if (!kTmaStore) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp's vectors are in registers
     }
-
-    mab = lane < nwarps ? red_max[lane] : (kHalfNegInf | (kHalfNegInf << 16));
-    mab = warp_max_h2(mab);
-    const float2 mf = __half22float2(bits_h2(mab));  // row maxima of the halves
-
-    // exp2((x - max) * scale*log2(e)) once per element, kept in registers.
-    // The difference comes first: it is 0 for the maximum (and for its ties)
-    // whatever the scale, and a product-then-subtract form would let the
-    // compiler fuse it into one FMA that keeps the product's rounding residual.
+    // Warp max (packed-half butterfly), then exp2 relative to it and the warp sum.
+    const uint32_t hmw = warp_max_h2(h2_bits(__halves2half2(hm, hm)));
+    const float mw = __low2float(bits_h2(hmw));
+    const float2 nm2 = make_float2(-mw, -mw);
     float e[V][8];
-    float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int v = tid + j * T;
-      if (v < nv) {
-        const bool in_a = v < na;
-        const int32_t lim = in_a ? va - v * 8 : vb - (v - na) * 8;
-        const float nm = in_a ? -mf.x : -mf.y;
-        const float2 nm2 = make_float2(nm, nm);
-        const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+      const int32_t v = v0 + 32 * j;
+      if (active && v < n_row) {
+        const uint32_t w4[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w[q])), nm2), sl2);
+          const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[q])), nm2), sl2);
           e[j][2 * q] = ex2(d.x);
           e[j][2 * q + 1] = ex2(d.y);
         }
+        const int32_t lim = valid - v * 8;
         if (lim < 8) {
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             if (q >= lim) e[j][q] = 0.f;
         }
-        const float2 acc = __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
-                                      __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7])));
-        if (in_a) sa = __fadd2_rn(sa, acc); else sb = __fadd2_rn(sb, acc);
+        acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
+                                         __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7]))));
       }
     }
-    float2 sm = warp_sum2(make_float2(sa.x + sa.y, sb.x + sb.y));
-    if (lane == 0) red_sum[warp] = sm;
-    __syncthreads();  // partial sums published
-    float2 q = lane < nwarps ? red_sum[lane] : make_float2(0.f, 0.f);
-    q = warp_sum2(q);
-    const float inv_a = rcp_rn(q.x);
-    const float inv_b = rcp_rn(q.y);
+    const float sw = warp_sum(acc.x + acc.y);
+    float2* rk = red + (k & 1) * 32;
+    if (lane == 0) rk[warp] = active ? make_float2(mw, sw) : make_float2(-INFINITY, 0.f);
+    asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumer warps only
+    if (*abort_flag) break;
 
+    // Merge the partials of this row's warps: M, S, and this warp's factor.
+    const int32_t w_first = row_a ? 0 : wa, w_count = row_a ? wa : wb;
+    float M = -INFINITY, Ssum = 0.f;
+    for (int32_t i = 0; i < w_count; ++i) {
+      const float2 ps = rk[w_first + i];
+      merge_ms(M, Ssum, ps.x, ps.y, sl);
+    }
+    const float c = ex2((mw - M) * sl) * rcp_rn(Ssum);
+    const float2 c2 = make_float2(c, c);
+
+    uint16_t* out_row = g.out + (int64_t)b * g.batch_stride + (int64_t)(row_a ? ra : rb) * g.pitch;
+    uint8_t* st_out = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int v = tid + j * T;
-      if (v < nv) {
-        const bool in_a = v < na;
-        const float inv = in_a ? inv_a : inv_b;
-        const float2 inv2 = make_float2(inv, inv);
+      const int32_t v = v0 + 32 * j;
+      if (active && v < n_row) {
         uint32_t o[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float2 pr = __fmul2_rn(make_float2(e[j][2 * c], e[j][2 * c + 1]), inv2);
-          o[c] = float2_to_half2_bits(pr.x, pr.y);
+        for (int q = 0; q < 4; ++q) {
+          const float2 pr = __fmul2_rn(make_float2(e[j][2 * q], e[j][2 * q + 1]), c2);
+          o[q] = float2_to_half2_bits(pr.x, pr.y);
         }
         const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
-        if (kTmaStore) {
-          *reinterpret_cast<uint4*>(stage_base + (size_t)s * p.stage_bytes + (size_t)v * 16) = ov;
-        } else {
-          uint16_t* dst = in_a ? row_a + (int64_t)v * 8 : row_b + (int64_t)(v - na) * 8;
-          *reinterpret_cast<uint4*>(dst) = ov;
-        }
+        if (kTmaStore)
+          *reinterpret_cast<uint4*>(st_out + (size_t)v * 16) = ov;
+        else
+          *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = ov;
       }
     }
     if (kTmaStore) {
-      fence_proxy_async_smem();  // make this thread's stage writes visible to the bulk copy
-      __syncthreads();
-      if (tid == 0) {
-        uint8_t* st_out = stage_base + (size_t)s * p.stage_bytes;
-        bulk_s2g(row_a, st_out, (uint32_t)na * 16u);
-        if (rb >= 0) bulk_s2g(row_b, st_out + (size_t)na * 16, (uint32_t)nb * 16u);
-        bulk_commit();
-      }
+      fence_proxy_async_smem();  // outputs visible to the bulk-store engine
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (!p.zero_tma) {
-      // Masked columns and pitch padding: 16-byte zero stores, no loads.
-      const int32_t za = pv - na;
-      const int32_t zb = rb >= 0 ? pv - nb : 0;
-      for (int32_t zi = tid; zi < za + zb; zi += T) {
-        uint16_t* dst = zi < za ? row_a + (int64_t)(na + zi) * 8 : row_b + (int64_t)(nb + zi - za) * 8;
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      // Masked columns and pitch padding by this warp's lanes (no loads).
+      if (active && seg == 0) {
+        for (int32_t zi = n_row + lane; zi < pv; zi += 32)
+          *reinterpret_cast<uint4*>(out_row + (int64_t)zi * 8) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    advance(cb, ck);
-  }
-
-  // Bulk stores must finish reading shared memory before the CTA exits.
-  if ((kTmaStore || p.zero_tma) && tid == 0) bulk_wait_all();
-
-  // After a timeout: let this CTA's own copies in flight land (bounded)
-  // before the shared memory they target is released.
-  if (tid == 0 && k < n_mine) {
-    for (int32_t r = k; r < n_issued; ++r)
-      (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+    kk += gr;
+    b += gq;
+    if (kk >= upm) {
+      kk -= upm;
+      ++b;
+    }
+    if (++s == S) {
+      s = 0;
+      parity ^= 1u;
+    }
   }
 }
 
