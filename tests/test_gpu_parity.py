@@ -246,9 +246,10 @@ def test_row_resident_tuning_variants(tuning):
 
 
 def test_unpaired_fallback_when_a_pair_does_not_fit():
-    # Forcing 2 vectors per thread caps a unit at 2048 vectors: row pairs of
-    # ~32000 columns do not fit, single rows do, so the planner drops pairing.
-    rows, cols, off = 40, 16384, 16000
+    # Forcing 2 vectors per thread caps a unit at 30 warps x 64 vectors: row
+    # pairs of ~24000 columns do not fit, single rows (~1500 vectors) do, so
+    # the planner drops pairing.
+    rows, cols, off = 40, 12288, 12000
     x = cs.generate(5, 4, batch=1, rows=rows, cols=cols, first_row=off)[0]
     d_in = to_dev(x)
     d_out = sentinel_like(d_in)
