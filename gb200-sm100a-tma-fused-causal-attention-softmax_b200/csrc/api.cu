@@ -78,24 +78,24 @@ void* rowres_fn() {
   return reinterpret_cast<void*>(&cs::rowres_kernel<V, MAXT, TS>);
 }
 
-// Maximum CTA size (consumer warps + the producer warp) per vectors-per-thread
-// choice V of the row-resident kernel, which fixes its register budget:
-// V = 2 up to 1024 threads (64 registers), V = 4 up to 512 (128), V = 8 up
-// to 576 (96; long single rows of up to 32768 columns).
-constexpr int rowres_maxt(int v) { return v == 8 ? 576 : (v == 4 ? 512 : 1024); }
+// Instantiations of the row-resident kernel: V vectors per consumer lane and
+// the maximum CTA size (consumer warps + the producer warp), which fixes the
+// register budget. V = 8 with up to 256 threads (255 registers) is the
+// default; V = 8 with up to 576 threads (96 registers) serves single rows of
+// up to 32768 columns; V = 4 / 2 spread a unit over more warps.
+struct RowVariant {
+  int vec;
+  int maxt;
+};
+constexpr RowVariant kRowVariants[4] = {{8, 256}, {8, 576}, {4, 512}, {2, 1024}};
+constexpr int kNumRowVariants = 4;
 
-void* rowres_kernel_ptr(int v, bool tma_store) {
-  if (tma_store) {
-    switch (v) {
-      case 2: return rowres_fn<2, 1024, true>();
-      case 4: return rowres_fn<4, 512, true>();
-      default: return rowres_fn<8, 576, true>();
-    }
-  }
-  switch (v) {
-    case 2: return rowres_fn<2, 1024, false>();
-    case 4: return rowres_fn<4, 512, false>();
-    default: return rowres_fn<8, 576, false>();
+void* rowres_kernel_ptr(int variant, bool tma_store) {
+  switch (variant) {
+    case 0: return tma_store ? rowres_fn<8, 256, true>() : rowres_fn<8, 256, false>();
+    case 1: return tma_store ? rowres_fn<8, 576, true>() : rowres_fn<8, 576, false>();
+    case 2: return tma_store ? rowres_fn<4, 512, true>() : rowres_fn<4, 512, false>();
+    default: return tma_store ? rowres_fn<2, 1024, true>() : rowres_fn<2, 1024, false>();
   }
 }
 
@@ -125,7 +125,7 @@ int device_info(int dev, DeviceInfo** out) {
     DeviceGuard guard(dev);
     if (!guard.ok()) return CS_ERR_DEVICE;
     for (int ts = 0; ts < 2; ++ts)
-      for (int v : {2, 4, 8})
+      for (int v = 0; v < kNumRowVariants; ++v)
         CS_CUDA(cudaFuncSetAttribute(rowres_kernel_ptr(v, ts != 0),
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel),
@@ -177,7 +177,7 @@ struct Tuning {
 
 struct LaunchPlan {
   int kernel = 0;
-  int grid = 0, block = 0, smem = 0, stages = 0, vec = 0, ctas_per_sm = 0;
+  int grid = 0, block = 0, smem = 0, stages = 0, vec = 0, variant = 0, ctas_per_sm = 0;
   int64_t units = 0;
   int narrow_lanes = 0;
   cs::RowResParams rr{};
@@ -194,16 +194,17 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
   return mx;
 }
 
-// Vectors per thread and CTA size for units of up to max_nv vectors. Each
+// Kernel variant and CTA size for units of up to max_nv vectors. Each
 // consumer warp owns 32*V vectors of one row; a row pair needs one warp more
-// than its total in the worst split. One producer warp is added.
-bool rowres_shape(int64_t max_nv, bool paired, int want_vec, int* vec, int* block) {
-  const int order[3] = {4, 8, 2};
-  for (int v : order) {
+// than its total in the worst split. One producer warp is added. Variants
+// are tried in kRowVariants order (V = 8 first: the fewest warps per unit).
+bool rowres_shape(int64_t max_nv, bool paired, int want_vec, int* variant, int* block) {
+  for (int i = 0; i < kNumRowVariants; ++i) {
+    const int v = kRowVariants[i].vec;
     if (want_vec && v != want_vec) continue;
     const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
-    if (warps <= 31 && 32 * warps <= rowres_maxt(v)) {
-      *vec = v;
+    if (warps <= 31 && 32 * warps <= kRowVariants[i].maxt) {
+      *variant = i;
       *block = (int)(32 * warps);
       return true;
     }
@@ -216,13 +217,14 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
                 LaunchPlan* lp) {
   cs::UnitMap m = cs::make_unit_map(g, true);
   int64_t max_nv = rowres_max_vectors(g, m);
-  int vec = 0, block = 0;
-  if (!rowres_shape(max_nv, m.n_pairs > 0, t.vec, &vec, &block)) {
+  int variant = -1, block = 0;
+  if (!rowres_shape(max_nv, m.n_pairs > 0, t.vec, &variant, &block)) {
     // A pair may not fit where a single row still does.
     m = cs::make_unit_map(g, false);
     max_nv = rowres_max_vectors(g, m);
-    rowres_shape(max_nv, false, t.vec, &vec, &block);
+    rowres_shape(max_nv, false, t.vec, &variant, &block);
   }
+  const int vec = variant >= 0 ? kRowVariants[variant].vec : 0;
   if (!vec) {
     std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: %lld vectors per unit do not fit",
                   (long long)max_nv);
@@ -239,7 +241,7 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
     return CS_ERR_UNSUPPORTED;
   }
   int per_sm = 0;
-  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(vec, tma_store),
+  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(variant, tma_store),
                                                         block, smem));
   if (per_sm < 1) {
     std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: no resident CTA (block %d, smem %d)",
@@ -253,12 +255,14 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
   lp->smem = smem;
   lp->stages = stages;
   lp->vec = vec;
+  lp->variant = variant;
   lp->ctas_per_sm = per_sm;
   lp->rr.g = g;
   lp->rr.m = m;
   lp->rr.stages = stages;
   lp->rr.stage_bytes = stage_bytes;
-  lp->rr.l2_hint = t.hint < 0 ? 1 : t.hint;
+  // Measured on B200: the evict-first hint on the input copies costs ~3%.
+  lp->rr.l2_hint = t.hint < 0 ? 0 : t.hint;
   lp->rr.zero_tma = t.zero_tma < 0 ? 1 : t.zero_tma;
   return CS_OK;
 }
@@ -344,15 +348,23 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
     case CS_KERNEL_TMA:
     case CS_KERNEL_PIPELINE: {
       const bool ts = lp.kernel == CS_KERNEL_PIPELINE;
-      if (lp.vec == 2) {
-        if (ts) cs::rowres_kernel<2, 1024, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<2, 1024, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-      } else if (lp.vec == 4) {
-        if (ts) cs::rowres_kernel<4, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<4, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-      } else {
-        if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-        else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+      switch (lp.variant) {
+        case 0:
+          if (ts) cs::rowres_kernel<8, 256, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          else cs::rowres_kernel<8, 256, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          break;
+        case 1:
+          if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          break;
+        case 2:
+          if (ts) cs::rowres_kernel<4, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          else cs::rowres_kernel<4, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          break;
+        default:
+          if (ts) cs::rowres_kernel<2, 1024, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          else cs::rowres_kernel<2, 1024, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
+          break;
       }
       break;
     }
@@ -543,8 +555,8 @@ int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols) {
   if (kernel != CS_KERNEL_AUTO) return kernel;
   if (cols <= 32) return CS_KERNEL_WARP;
   // Host-side rule equal to make_plan's: the row-resident kernel takes any
-  // shape whose widest unit (a row pair, else a single row) fits 512 threads
-  // x 8 vectors and two stages of shared memory.
+  // shape whose widest unit (a row pair, else a single row) fits one of its
+  // variants (at most 576 threads x 8 vectors) and two stages of shared memory.
   Geometry g{};
   g.batch = 1;
   g.rows = (int32_t)std::min<int64_t>(rows, kI32Max);

@@ -54,19 +54,6 @@ __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
   return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
 }
 
-// Online-softmax merge of (m2, s2) into (m, s); empty states have m = -inf.
-__device__ __forceinline__ void merge_ms(float& m, float& s, float m2, float s2, float sl) {
-  if (m2 == -INFINITY) return;
-  if (m == -INFINITY) {
-    m = m2;
-    s = s2;
-    return;
-  }
-  const float mn = fmaxf(m, m2);
-  s = s * ex2((m - mn) * sl) + s2 * ex2((m2 - mn) * sl);
-  m = mn;
-}
-
 template <int V, int MAXT, bool kTmaStore>
 __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ RowResParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -227,16 +214,23 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     }
     const uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
 
+    // Vector slot j is skipped by the whole warp when its first lane is past
+    // the row (a warp-uniform test). Lanes past the row's end in the last
+    // slot, and the masked elements of the row's last vector, hold -inf
+    // halves: they lose the max and give exp 0 with no further masking.
+    const int32_t seg_first = seg * kSeg;  // warp-uniform
+    constexpr uint32_t kNeg2 = kHalfNegInf | (kHalfNegInf << 16);
     uint4 raw[V];
     __half hm = __ushort_as_half((unsigned short)kHalfNegInf);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int32_t v = v0 + 32 * j;
-      raw[j] = make_uint4(0u, 0u, 0u, 0u);
-      if (ok && active && v < n_row) {
-        raw[j] = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
-        const int32_t lim = valid - v * 8;
-        hm = __hmax(hm, max8_half(lim < 8 ? mask_tail_neg_inf(raw[j], lim) : raw[j]));
+      raw[j] = make_uint4(kNeg2, kNeg2, kNeg2, kNeg2);
+      if (ok && active && seg_first + 32 * j < n_row) {
+        const int32_t v = v0 + 32 * j;
+        const int32_t lim = valid - v * 8;  // <= 0 past the row's end
+        if (lim > 0) raw[j] = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
+        if (lim < 8) raw[j] = mask_tail_neg_inf(raw[j], lim);
+        hm = __hmax(hm, max8_half(raw[j]));
       }
     }
     if (!kTmaStore) {
@@ -249,25 +243,36 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     const float2 nm2 = make_float2(-mw, -mw);
     float e[V][8];
     float2 acc = make_float2(0.f, 0.f);
+    if (sl != 0.f) {
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      const int32_t v = v0 + 32 * j;
-      if (active && v < n_row) {
-        const uint32_t w4[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+      for (int j = 0; j < V; ++j) {
+        if (active && seg_first + 32 * j < n_row) {
+          const uint32_t w4[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[q])), nm2), sl2);
-          e[j][2 * q] = ex2(d.x);
-          e[j][2 * q + 1] = ex2(d.y);
+          for (int q = 0; q < 4; ++q) {
+            // -inf halves: (-inf - mw) * sl = -inf for sl > 0, so exp is 0.
+            const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[q])), nm2), sl2);
+            e[j][2 * q] = ex2(d.x);
+            e[j][2 * q + 1] = ex2(d.y);
+          }
+          acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
+                                           __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7]))));
         }
-        const int32_t lim = valid - v * 8;
-        if (lim < 8) {
+      }
+    } else {
+      // Zero scale: every causal element is exp(0) = 1 (uniform distribution).
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (q >= lim) e[j][q] = 0.f;
+      for (int j = 0; j < V; ++j) {
+        if (active && seg_first + 32 * j < n_row) {
+          const uint32_t w4[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            e[j][2 * q] = (w4[q] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
+            e[j][2 * q + 1] = (w4[q] >> 16) == kHalfNegInf ? 0.f : 1.f;
+          }
+          acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
+                                           __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7]))));
         }
-        acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(make_float2(e[j][0], e[j][1]), make_float2(e[j][2], e[j][3])),
-                                         __fadd2_rn(make_float2(e[j][4], e[j][5]), make_float2(e[j][6], e[j][7]))));
       }
     }
     const float sw = warp_sum(acc.x + acc.y);
@@ -276,13 +281,12 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumer warps only
     if (*abort_flag) break;
 
-    // Merge the partials of this row's warps: M, S, and this warp's factor.
+    // Merge the partials of this row's warps (lane i holds warp i's): the
+    // row max M, the rescaled sum S, and this warp's factor 2^((mw-M)sl)/S.
     const int32_t w_first = row_a ? 0 : wa, w_count = row_a ? wa : wb;
-    float M = -INFINITY, Ssum = 0.f;
-    for (int32_t i = 0; i < w_count; ++i) {
-      const float2 ps = rk[w_first + i];
-      merge_ms(M, Ssum, ps.x, ps.y, sl);
-    }
+    const float2 ps = lane < w_count ? rk[w_first + lane] : make_float2(-INFINITY, 0.f);
+    const float M = warp_max(ps.x);
+    const float Ssum = warp_sum(lane < w_count ? ps.y * ex2((ps.x - M) * sl) : 0.f);
     const float c = ex2((mw - M) * sl) * rcp_rn(Ssum);
     const float2 c2 = make_float2(c, c);
 
@@ -290,8 +294,8 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
     uint8_t* st_out = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int32_t v = v0 + 32 * j;
-      if (active && v < n_row) {
+      if (active && seg_first + 32 * j < n_row) {
+        const int32_t v = v0 + 32 * j;
         uint32_t o[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -299,10 +303,12 @@ __global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ Ro
           o[q] = float2_to_half2_bits(pr.x, pr.y);
         }
         const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
-        if (kTmaStore)
-          *reinterpret_cast<uint4*>(st_out + (size_t)v * 16) = ov;
-        else
-          *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = ov;
+        if (v < n_row) {
+          if (kTmaStore)
+            *reinterpret_cast<uint4*>(st_out + (size_t)v * 16) = ov;
+          else
+            *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = ov;
+        }
       }
     }
     if (kTmaStore) {
