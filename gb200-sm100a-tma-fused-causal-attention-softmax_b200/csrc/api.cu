@@ -73,29 +73,38 @@ class DeviceGuard {
   bool ok_ = true;
 };
 
-template <int V, int MAXT, bool TS>
-void* rowres_fn() {
-  return reinterpret_cast<void*>(&cs::rowres_kernel<V, MAXT, TS>);
-}
+// Instantiations of the row-resident kernel (index, V vectors per consumer
+// lane, launch bounds MAXT threads / MINB resident CTAs per SM, which set the
+// register budget). The planner tries them in kRowOrder: more resident warps
+// per SM hide the per-unit latency (shuffle butterflies, the barrier) best.
+#define CS_ROW_VARIANTS(X) \
+  X(0, 8, 256, 1)          \
+  X(1, 8, 576, 1)          \
+  X(2, 4, 512, 1)          \
+  X(3, 2, 1024, 1)         \
+  X(4, 4, 224, 4)          \
+  X(5, 2, 352, 3)
 
-// Instantiations of the row-resident kernel: V vectors per consumer lane and
-// the maximum CTA size (consumer warps + the producer warp), which fixes the
-// register budget. V = 8 with up to 256 threads (255 registers) is the
-// default; V = 8 with up to 576 threads (96 registers) serves single rows of
-// up to 32768 columns; V = 4 / 2 spread a unit over more warps.
 struct RowVariant {
   int vec;
   int maxt;
+  int minb;
 };
-constexpr RowVariant kRowVariants[4] = {{8, 256}, {8, 576}, {4, 512}, {2, 1024}};
-constexpr int kNumRowVariants = 4;
+#define CS_ROW_ENTRY(i, v, t, b) {v, t, b},
+constexpr RowVariant kRowVariants[] = {CS_ROW_VARIANTS(CS_ROW_ENTRY)};
+#undef CS_ROW_ENTRY
+constexpr int kNumRowVariants = (int)(sizeof(kRowVariants) / sizeof(kRowVariants[0]));
+constexpr int kRowOrder[kNumRowVariants] = {4, 2, 0, 1, 5, 3};
 
-void* rowres_kernel_ptr(int variant, bool tma_store) {
+void* rowres_kernel_ptr(int variant, bool ts) {
   switch (variant) {
-    case 0: return tma_store ? rowres_fn<8, 256, true>() : rowres_fn<8, 256, false>();
-    case 1: return tma_store ? rowres_fn<8, 576, true>() : rowres_fn<8, 576, false>();
-    case 2: return tma_store ? rowres_fn<4, 512, true>() : rowres_fn<4, 512, false>();
-    default: return tma_store ? rowres_fn<2, 1024, true>() : rowres_fn<2, 1024, false>();
+#define CS_ROW_PTR(i, v, t, b)                                                          \
+  case i:                                                                               \
+    return ts ? reinterpret_cast<void*>(&cs::rowres_kernel<v, t, b, true>)              \
+              : reinterpret_cast<void*>(&cs::rowres_kernel<v, t, b, false>);
+    CS_ROW_VARIANTS(CS_ROW_PTR)
+#undef CS_ROW_PTR
+    default: return nullptr;
   }
 }
 
@@ -197,11 +206,13 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
 // Kernel variant and CTA size for units of up to max_nv vectors. Each
 // consumer warp owns 32*V vectors of one row; a row pair needs one warp more
 // than its total in the worst split. One producer warp is added. Variants
-// are tried in kRowVariants order (V = 8 first: the fewest warps per unit).
+// are tried in kRowOrder; want_vec in {2, 4, 8} restricts V, and
+// want_vec = 16 + i asks for variant i.
 bool rowres_shape(int64_t max_nv, bool paired, int want_vec, int* variant, int* block) {
-  for (int i = 0; i < kNumRowVariants; ++i) {
+  for (int n = 0; n < kNumRowVariants; ++n) {
+    const int i = kRowOrder[n];
     const int v = kRowVariants[i].vec;
-    if (want_vec && v != want_vec) continue;
+    if (want_vec >= 16 ? want_vec - 16 != i : (want_vec && v != want_vec)) continue;
     const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
     if (warps <= 31 && 32 * warps <= kRowVariants[i].maxt) {
       *variant = i;
@@ -349,22 +360,14 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
     case CS_KERNEL_PIPELINE: {
       const bool ts = lp.kernel == CS_KERNEL_PIPELINE;
       switch (lp.variant) {
-        case 0:
-          if (ts) cs::rowres_kernel<8, 256, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          else cs::rowres_kernel<8, 256, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          break;
-        case 1:
-          if (ts) cs::rowres_kernel<8, 576, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          else cs::rowres_kernel<8, 576, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          break;
-        case 2:
-          if (ts) cs::rowres_kernel<4, 512, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          else cs::rowres_kernel<4, 512, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          break;
-        default:
-          if (ts) cs::rowres_kernel<2, 1024, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          else cs::rowres_kernel<2, 1024, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);
-          break;
+#define CS_ROW_LAUNCH(i, v, t, b)                                                          \
+  case i:                                                                                  \
+    if (ts) cs::rowres_kernel<v, t, b, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr); \
+    else cs::rowres_kernel<v, t, b, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);   \
+    break;
+        CS_ROW_VARIANTS(CS_ROW_LAUNCH)
+#undef CS_ROW_LAUNCH
+        default: return CS_ERR_BAD_KERNEL;
       }
       break;
     }
@@ -653,7 +656,9 @@ int cs_plan_set_timeout(cs_plan* plan, uint64_t timeout_ns) {
 
 int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint, int zero_fill_tma) {
   if (!plan) return CS_ERR_NULL;
-  if (vec_per_thread != 0 && vec_per_thread != 2 && vec_per_thread != 4 && vec_per_thread != 8)
+  const bool variant_pick = vec_per_thread >= 16 && vec_per_thread < 16 + kNumRowVariants;
+  if (vec_per_thread != 0 && vec_per_thread != 2 && vec_per_thread != 4 && vec_per_thread != 8 &&
+      !variant_pick)
     return CS_ERR_ARG;
   if (stages < 0 || stages > 24 || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
   if (zero_fill_tma < -1 || zero_fill_tma > 1) return CS_ERR_ARG;

@@ -54,8 +54,10 @@ __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
   return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
 }
 
-template <int V, int MAXT, bool kTmaStore>
-__global__ void __launch_bounds__(MAXT) rowres_kernel(const __grid_constant__ RowResParams p) {
+// V: 16-byte vectors per consumer lane; MAXT / MINB: launch bounds (CTA
+// size and resident CTAs per SM), which set the register budget.
+template <int V, int MAXT, int MINB, bool kTmaStore>
+__global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constant__ RowResParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Geometry& g = p.g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;

@@ -166,7 +166,8 @@ int cs_plan_status(cs_plan *plan, uint32_t *status);
 int cs_plan_set_timeout(cs_plan *plan, uint64_t timeout_ns);
 
 /* Tuning knobs (0 / -1 = automatic): vectors per thread of the TMA /
- * PIPELINE kernels (2, 4 or 8), ring stages of the TMA / PIPELINE / ONLINE
+ * PIPELINE kernels (2, 4 or 8; 16 + i selects compiled variant i of the
+ * row-resident kernel directly), ring stages of the TMA / PIPELINE / ONLINE
  * kernels (1..24), L2 evict-first hint on the input copies (0 off, 1 on),
  * masked columns written by TMA bulk stores (1) or by thread stores (0). */
 int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint,
