@@ -210,6 +210,30 @@ __device__ __forceinline__ uint32_t warp_max_h2(uint32_t v) {
   return v;
 }
 
+// Single-instruction warp reductions (sm_100a redux.sync).
+__device__ __forceinline__ float redux_max(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t redux_add(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// Warp sum of non-negative x <= 2^31 / 2^kShift, in fixed point with kShift
+// fractional bits: each lane is rounded to 2^-(kShift+1), split into two
+// 16-bit halves whose sums cannot overflow, and reduced with two integer
+// redux instructions. Integers (zero-scale counts) are summed exactly.
+template <int kShift>
+__device__ __forceinline__ float warp_sum_fixed(float x) {
+  const uint32_t q = __float2uint_rn(x * (float)(1u << kShift));
+  const uint32_t hi = redux_add(q >> 16), lo = redux_add(q & 0xFFFFu);
+  return ((float)hi * 65536.f + (float)lo) * (1.f / (float)(1u << kShift));
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -239,9 +239,8 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // this warp's vectors are in registers
     }
-    // Warp max (packed-half butterfly), then exp2 relative to it and the warp sum.
-    const uint32_t hmw = warp_max_h2(h2_bits(__halves2half2(hm, hm)));
-    const float mw = __low2float(bits_h2(hmw));
+    // Warp max (one redux instruction), then exp2 relative to it and the warp sum.
+    const float mw = redux_max(__half2float(hm));
     const float2 nm2 = make_float2(-mw, -mw);
     float e[V][8];
     float2 acc = make_float2(0.f, 0.f);
@@ -277,7 +276,8 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
         }
       }
     }
-    const float sw = warp_sum(acc.x + acc.y);
+    // A lane's partial sum is at most 8V <= 64: 25 fractional bits fit.
+    const float sw = warp_sum_fixed<25>(acc.x + acc.y);
     float2* rk = red + (k & 1) * 32;
     if (lane == 0) rk[warp] = active ? make_float2(mw, sw) : make_float2(-INFINITY, 0.f);
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumer warps only
@@ -287,8 +287,9 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
     // row max M, the rescaled sum S, and this warp's factor 2^((mw-M)sl)/S.
     const int32_t w_first = row_a ? 0 : wa, w_count = row_a ? wa : wb;
     const float2 ps = lane < w_count ? rk[w_first + lane] : make_float2(-INFINITY, 0.f);
-    const float M = warp_max(ps.x);
-    const float Ssum = warp_sum(lane < w_count ? ps.y * ex2((ps.x - M) * sl) : 0.f);
+    const float M = redux_max(ps.x);
+    // A warp's sum is at most 32 * 64 = 2^11: 20 fractional bits fit.
+    const float Ssum = warp_sum_fixed<20>(lane < w_count ? ps.y * ex2((ps.x - M) * sl) : 0.f);
     const float c = ex2((mw - M) * sl) * rcp_rn(Ssum);
     const float2 c2 = make_float2(c, c);
 
