@@ -1,0 +1,107 @@
+"""Multi-rank host path on CPU (gloo, world_size 2): the sharding bench.py uses.
+
+Each rank regenerates only its shard (heads via first_batch, row blocks via
+first_row), computes it with the oracle standing in for the device kernel
+(row_offset = absolute first row), and the shards gathered on rank 0 must equal
+the unsharded result bit for bit. Also checks the max-over-ranks timing
+reduction and that row blocks are balanced by causal cost.
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, q):
+    import bench
+    import causal_softmax as cs
+    import oracle_ctypes as O
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # Row blocks of one matrix (the single-matrix workloads).
+        rows, cols = 300, 260
+        pitch = cs.padded_pitch(cols)
+        a, b = bench.row_blocks(rows, cols, world)[rank]
+        x = cs.generate(3, 2, batch=1, rows=b - a, cols=cols, first_row=a)[0]
+        y = O.softmax_strided(x.ravel(), 1, 0, b - a, cols, pitch, a, 1.0).reshape(b - a, pitch)
+        parts = [None] * world
+        dist.all_gather_object(parts, (a, b, y))
+        # Heads (the batched workload).
+        heads, hr = 6, 40
+        hp = cs.padded_pitch(hr)
+        per = heads // world
+        xh = cs.generate(4, 3, batch=per, rows=hr, cols=hr, first_batch=rank * per)
+        yh = O.softmax_strided(xh.ravel(), per, hr * hp, hr, hr, hp, 0, 0.0883883).reshape(per, hr, hp)
+        hparts = [None] * world
+        dist.all_gather_object(hparts, yh)
+        # Max over ranks, as bench.py reduces its step times.
+        t = torch.tensor([float(rank + 1)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            q.put((parts, hparts, float(t.item())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_results_equal_unsharded():
+    import bench
+    import causal_softmax as cs
+    import oracle_ctypes as O
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    parts, hparts, tmax = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert tmax == float(world)
+
+    rows, cols = 300, 260
+    pitch = cs.padded_pitch(cols)
+    x = cs.generate(3, 2, batch=1, rows=rows, cols=cols)[0]
+    full = O.softmax_strided(x.ravel(), 1, 0, rows, cols, pitch, 0, 1.0).reshape(rows, pitch)
+    assert [p[0] for p in parts] == [0, parts[0][1]] and parts[-1][1] == rows
+    assert np.array_equal(np.concatenate([p[2] for p in parts]), full)
+
+    heads, hr = 6, 40
+    hp = cs.padded_pitch(hr)
+    xh = cs.generate(4, 3, batch=heads, rows=hr, cols=hr)
+    fh = O.softmax_strided(xh.ravel(), heads, hr * hp, hr, hr, hp, 0, 0.0883883).reshape(heads, hr, hp)
+    assert np.array_equal(np.concatenate(hparts), fh)
+
+
+def test_row_blocks_balance_causal_cost():
+    import bench
+
+    for rows, cols, parts in [(4096, 4096, 2), (4096, 4096, 8), (32768, 32768, 8), (1000, 1037, 4),
+                              (4096, 32, 8), (7, 100, 8)]:
+        blocks = bench.row_blocks(rows, cols, parts)
+        assert len(blocks) == parts and blocks[0][0] == 0 and blocks[-1][1] == rows
+        assert all(b[0] <= b[1] for b in blocks)
+        assert all(blocks[i][1] == blocks[i + 1][0] for i in range(parts - 1))
+        cost = lambda a, b: sum(2 * min(r + 1, cols) + 2 * cols for r in range(a, b))
+        costs = [cost(a, b) for a, b in blocks]
+        row_cost = 2 * cols + 2 * min(rows, cols)
+        if rows >= 8 * parts:
+            assert max(costs) - min(costs) <= 2 * row_cost, (rows, cols, parts, costs)
