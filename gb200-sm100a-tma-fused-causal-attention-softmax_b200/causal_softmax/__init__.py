@@ -138,6 +138,8 @@ def _declare(L) -> None:
         "cs_softmax": (c_int, [c_int, vp, vp, c_i32, c_i32, c_i32, c_f32, vp]),
         "cs_softmax_batched": (c_int, [c_int, vp, vp, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32,
                                        c_f32, vp]),
+        "cs_softmax_noalloc": (c_int, [c_int, vp, vp, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32,
+                                       c_f32, c_i32, ctypes.POINTER(ctypes.c_uint32), vp]),
         "cs_session_create": (c_int, [ctypes.POINTER(vp), c_int]),
         "cs_session_probe": (c_int, [vp]),
         "cs_session_softmax_host": (c_int, [vp, c_int, u16p, u16p, c_i64, c_i32, c_i32, c_i32,

@@ -51,6 +51,7 @@ struct DeviceInfo {
   int major = 0, minor = 0;
   int max_smem_optin = 0;
   uint32_t* oneshot_status = nullptr;  // status word for cs_softmax*
+  uint32_t* noalloc_status = nullptr;  // device address of g_noalloc_status
   bool attrs_set = false;
 };
 
@@ -767,6 +768,81 @@ int cs_softmax_batched(int kernel, const void* d_in, void* d_out, int64_t batch,
 int cs_softmax(int kernel, const void* d_in, void* d_out, int32_t rows, int32_t cols, int32_t pitch,
                float scale, void* stream) {
   return cs_softmax_batched(kernel, d_in, d_out, 1, 0, rows, cols, pitch, 0, scale, stream);
+}
+
+// ===========================================================================
+// One-shot launch that allocates nothing
+// ===========================================================================
+
+// The status words of cs_softmax_noalloc, one per slot. They live in the
+// library's device image rather than in cudaMalloc'd memory, so that entry
+// point never allocates; every GPU that loads the library holds these
+// CS_NOALLOC_SLOTS * 4 = 256 bytes until the process exits. On the host the
+// name only stands in for the symbol: the device address comes from
+// cudaGetSymbolAddress.
+static __device__ __align__(256) uint32_t g_noalloc_status[CS_NOALLOC_SLOTS];
+
+namespace {
+
+// Device address of g_noalloc_status on `dev`, which must be the current
+// device. Looked up once per device, on that device's first call.
+int noalloc_status_for(int dev, uint32_t** out) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(dev, &d);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!d->noalloc_status) {
+    uint32_t* p = nullptr;
+    CS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_status));
+    d->noalloc_status = p;
+  }
+  *out = d->noalloc_status;
+  return CS_OK;
+}
+
+}  // namespace
+
+int cs_softmax_noalloc(int kernel, const void* d_in, void* d_out, int64_t batch, int64_t batch_stride,
+                       int32_t rows, int32_t cols, int32_t pitch, int32_t row_offset, float scale,
+                       int32_t slot, uint32_t* status, void* stream) {
+  int rc = validate_args(batch, batch_stride, rows, cols, pitch, row_offset, scale);
+  if (rc) return rc;
+  rc = check_pointers(d_in, d_out);
+  if (rc) return rc;
+  if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
+  if (slot < 0 || slot >= CS_NOALLOC_SLOTS) {
+    std::snprintf(t_detail, sizeof t_detail,
+                  "status slot %d out of range: the static status array holds %d words (slots 0..%d)",
+                  (int)slot, CS_NOALLOC_SLOTS, CS_NOALLOC_SLOTS - 1);
+    return CS_ERR_ARG;
+  }
+  int dev = 0;
+  CS_CUDA(cudaGetDevice(&dev));
+  uint32_t* words = nullptr;
+  rc = noalloc_status_for(dev, &words);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The word keeps the bits of the last call that used this slot.
+  CS_CUDA(cudaMemsetAsync(words + slot, 0, sizeof(uint32_t), s));
+  Geometry g{};
+  g.in = static_cast<const uint16_t*>(d_in);
+  g.out = static_cast<uint16_t*>(d_out);
+  g.batch = batch;
+  g.batch_stride = batch > 1 ? batch_stride : (int64_t)rows * pitch;
+  g.rows = rows;
+  g.cols = cols;
+  g.pitch = pitch;
+  g.row_offset = row_offset;
+  g.scale = scale;
+  g.status = words + slot;
+  g.timeout_ns = kDefaultTimeoutNs;
+  rc = launch_geometry(dev, kernel, g, Tuning{}, s, nullptr);
+  if (rc || !status) return rc;
+  uint32_t word = 0;
+  CS_CUDA(cudaMemcpyAsync(&word, words + slot, sizeof word, cudaMemcpyDeviceToHost, s));
+  CS_CUDA(cudaStreamSynchronize(s));
+  *status = word;
+  return (word & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
 }
 
 // ===========================================================================

@@ -209,6 +209,36 @@ int cs_softmax_batched(int kernel, const void *d_in, void *d_out, int64_t batch,
                        int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch,
                        int32_t row_offset, float scale, void *stream);
 
+/* No counterpart in the reference. cs_softmax_batched with the same arguments
+ * and results, for callers that may not allocate device memory: a serving
+ * engine or framework whose caching allocator owns the GPU's memory and
+ * budgets every byte, and which cannot let a library call cudaMalloc behind
+ * its back (cudaMalloc can synchronize the device and takes memory outside
+ * that budget). cs_softmax_batched allocates a 256-byte status word on its
+ * first call on each device; this entry point allocates nothing. Its only
+ * scratch is the kernels' status word, taken from a static device array of
+ * CS_NOALLOC_SLOTS 32-bit words (256 bytes) in the library's device image,
+ * which every GPU that loads the library holds until the process exits.
+ *
+ * `slot` picks the word (0 <= slot < CS_NOALLOC_SLOTS, else CS_ERR_ARG with a
+ * message). The call clears that word on `stream` before the launch, since it
+ * keeps the previous call's bits. Calls that overlap on the GPU and use the
+ * same slot race on it: one call's clear can erase the other's timeout bit.
+ * Callers that launch on several streams at once give each stream its own
+ * slot. If `status` is non-null the call waits for `stream`, stores the
+ * CS_STATUS_* bits there and returns CS_ERR_TIMEOUT if a bounded wait ran
+ * out; if it is null the call returns after the launch.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, which may load the library's device code); make that
+ * first call before any stream capture. Errors: as cs_softmax_batched, plus
+ * CS_ERR_ARG for a bad slot. */
+#define CS_NOALLOC_SLOTS 64
+int cs_softmax_noalloc(int kernel, const void *d_in, void *d_out, int64_t batch,
+                       int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch,
+                       int32_t row_offset, float scale, int32_t slot, uint32_t *status,
+                       void *stream);
+
 /* ---------------------------------------------------------------- */
 /* Sessions: host buffers (replaces gpu/src/driver.rs:12-59, 213-248) */
 /* ---------------------------------------------------------------- */
