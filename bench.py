@@ -91,9 +91,9 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def ncu_traffic_per_matrix(workload: str) -> float | None:
-    """DRAM bytes per matrix of the workload from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", f"tma_rowres_{workload}.md")
+def ncu_traffic_per_matrix(kernel: str, workload: str) -> float | None:
+    """DRAM bytes per matrix of the kernel on the workload, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
     try:
         for line in open(p):
             if line.strip().startswith("dram_bytes_per_matrix"):
@@ -384,7 +384,7 @@ def main() -> int:
 
     peak, peak_kind = measured_peak()
     achieved = alg_local / (ms_total / args.steps / 1e3) / 1e9
-    tpm = ncu_traffic_per_matrix(args.workload)
+    tpm = ncu_traffic_per_matrix(info["kernel_name"], args.workload)
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
                 "traffic": round(tpm * n_local * rows / rows_full) if tpm else None,

@@ -103,7 +103,7 @@ int cs_kernel_parse(const char *name);
 int cs_kernel_supports(int kernel, int64_t cols);
 
 /* host/src/lib.rs:169-177 (Config::resolved_kernel) for this library:
- * WARP for cols <= 32, TMA while a row pair fits the row-resident kernel,
+ * WARP for cols <= 32, PIPELINE while a row pair (else a row) fits the row-resident kernel,
  * ONLINE beyond. Non-AUTO values are returned unchanged. */
 int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols);
 

@@ -66,9 +66,9 @@ def test_supports_and_auto_dispatch():
     # host/src/lib.rs:169-177 (warp for cols <= 32), then this library's choice.
     assert cs.resolve_kernel("auto", 4096, 31) == "warp"
     assert cs.resolve_kernel("auto", 4096, 32) == "warp"
-    assert cs.resolve_kernel("auto", 4096, 4096) == "tma"
-    assert cs.resolve_kernel("auto", 32768, 32768) == "tma"
-    assert cs.resolve_kernel("auto", 8, 1 << 20) == "tma"  # only 8 causal columns per row
+    assert cs.resolve_kernel("auto", 4096, 4096) == "pipeline"
+    assert cs.resolve_kernel("auto", 32768, 32768) == "pipeline"
+    assert cs.resolve_kernel("auto", 8, 1 << 20) == "pipeline"  # only 8 causal columns per row
     assert cs.resolve_kernel("auto", 70000, 70000) == "online"
     assert cs.resolve_kernel("baseline", 4, 4) == "baseline"
 
@@ -212,7 +212,7 @@ def test_config_parse_mirrors_reference():
     c = cs.parse_config([])
     assert (c["rows"], c["cols"], c["scale"], c["iterations"], c["warmup"], c["verify"]) == \
         (4096, 4096, 0.125, 20, 5, 1)
-    assert cs.resolve_kernel(c["kernel"], c["rows"], c["cols"]) == "tma"
+    assert cs.resolve_kernel(c["kernel"], c["rows"], c["cols"]) == "pipeline"
     c = cs.parse_config(["--bench", "--rows", "12", "--cols", "17", "--scale", "0.5",
                          "--iterations", "7"])
     assert (c["action"], c["rows"], c["cols"], c["iterations"], c["scale"]) == (4, 12, 17, 7, 0.5)
