@@ -28,7 +28,8 @@ using cs::Geometry;
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s of GPU time per wait
 constexpr int kDefaultStages = 3;
-constexpr int64_t kRingBytesPerSm = 48 * 1024;  // row-resident ring bytes per SM for two stages
+constexpr int64_t kRingBytesPerSm = 72 * 1024;  // row-resident ring bytes per SM (target)
+constexpr int kMaxAutoStages = 8;
 constexpr int kOnlineDefaultStages = 8;
 constexpr int64_t kI32Max = 2147483647;
 constexpr int64_t kMaxUnitsPerLaunch = int64_t(1) << 30;  // row-resident kernel, 32-bit unit index
@@ -53,6 +54,7 @@ struct DeviceInfo {
   int max_smem_optin = 0;
   uint32_t* oneshot_status = nullptr;  // status word for cs_softmax*
   uint32_t* noalloc_status = nullptr;  // device address of g_noalloc_status
+  int row_regs[2][16] = {};            // registers per thread of each row-resident variant
   bool attrs_set = false;
 };
 
@@ -77,15 +79,16 @@ class DeviceGuard {
 
 // Instantiations of the row-resident kernel (index, V vectors per consumer
 // lane, launch bounds MAXT threads / MINB resident CTAs per SM, which set the
-// register budget). The planner tries them in kRowOrder: more resident warps
-// per SM hide the per-unit latency (shuffle butterflies, the barrier) best.
+// register budget). The planner picks among them by occupancy and register
+// budget (rowres_pick).
 #define CS_ROW_VARIANTS(X) \
   X(0, 8, 256, 1)          \
   X(1, 8, 576, 1)          \
   X(2, 4, 512, 1)          \
   X(3, 2, 1024, 1)         \
   X(4, 4, 224, 4)          \
-  X(5, 2, 352, 3)
+  X(5, 2, 352, 3)          \
+  X(6, 4, 384, 2)
 
 struct RowVariant {
   int vec;
@@ -96,7 +99,6 @@ struct RowVariant {
 constexpr RowVariant kRowVariants[] = {CS_ROW_VARIANTS(CS_ROW_ENTRY)};
 #undef CS_ROW_ENTRY
 constexpr int kNumRowVariants = (int)(sizeof(kRowVariants) / sizeof(kRowVariants[0]));
-constexpr int kRowOrder[kNumRowVariants] = {4, 2, 0, 1, 5, 3};
 
 void* rowres_kernel_ptr(int variant, bool ts) {
   switch (variant) {
@@ -136,9 +138,13 @@ int device_info(int dev, DeviceInfo** out) {
     DeviceGuard guard(dev);
     if (!guard.ok()) return CS_ERR_DEVICE;
     for (int ts = 0; ts < 2; ++ts)
-      for (int v = 0; v < kNumRowVariants; ++v)
+      for (int v = 0; v < kNumRowVariants; ++v) {
         CS_CUDA(cudaFuncSetAttribute(rowres_kernel_ptr(v, ts != 0),
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+        cudaFuncAttributes fa{};
+        CS_CUDA(cudaFuncGetAttributes(&fa, rowres_kernel_ptr(v, ts != 0)));
+        d.row_regs[ts][v] = fa.numRegs;
+      }
     CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     d.attrs_set = true;
@@ -205,37 +211,80 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
   return mx;
 }
 
-// Kernel variant and CTA size for units of up to max_nv vectors. Each
-// consumer warp owns 32*V vectors of one row; a row pair needs one warp more
-// than its total in the worst split. One producer warp is added. Variants
-// are tried in kRowOrder; want_vec in {2, 4, 8} restricts V, and
-// want_vec = 16 + i asks for variant i.
-bool rowres_shape(int64_t max_nv, bool paired, int want_vec, int* variant, int* block) {
-  for (int n = 0; n < kNumRowVariants; ++n) {
-    const int i = kRowOrder[n];
-    const int v = kRowVariants[i].vec;
-    if (want_vec >= 16 ? want_vec - 16 != i : (want_vec && v != want_vec)) continue;
-    const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
-    if (warps <= 31 && 32 * warps <= kRowVariants[i].maxt) {
-      *variant = i;
-      *block = (int)(32 * warps);
-      return true;
-    }
-  }
+// CTA size of variant i for units of up to max_nv vectors: each consumer
+// warp owns 32*V vectors of one row, a row pair needs one warp more than its
+// total in the worst split, and one producer warp is added. False if the
+// variant cannot hold such a unit.
+bool rowres_block(int64_t max_nv, bool paired, int i, int* block) {
+  const int v = kRowVariants[i].vec;
+  const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
+  if (warps > 31 || 32 * warps > kRowVariants[i].maxt) return false;
+  *block = (int)(32 * warps);
+  return true;
+}
+
+// Whether tuning vec `want_vec` admits variant i (0: any; 2, 4, 8: that V;
+// 16 + j: variant j only).
+bool rowres_wanted(int want_vec, int i) {
+  if (want_vec >= 16) return want_vec - 16 == i;
+  return !want_vec || kRowVariants[i].vec == want_vec;
+}
+
+// Host-only fit test (no device queries): some admitted variant holds the unit.
+bool rowres_shape(int64_t max_nv, bool paired, int want_vec) {
+  int block = 0;
+  for (int i = 0; i < kNumRowVariants; ++i)
+    if (rowres_wanted(want_vec, i) && rowres_block(max_nv, paired, i, &block)) return true;
   return false;
+}
+
+// Variant groups in order of preference: V = 4 first, then 8, then 2
+// (measured on B200 over square widths 1024..32768: V = 4 wins wherever it
+// fits; V = 8 only where it does not; V = 2 only below ~1500 columns).
+constexpr int kRowGroups[3][3] = {{4, 6, 2}, {0, 1, -1}, {5, 3, -1}};
+
+// Pick the variant for units of up to max_nv vectors. Within a group the
+// score is resident warps per SM x registers^1.5: more resident warps hide
+// the per-unit latency, but a variant with a smaller register budget (and
+// spills) must buy about 30% more warps to win (measured: 2048-wide rows run
+// 7% faster on 4 CTAs x 87 registers than on 5 CTAs x 72).
+int rowres_pick(const DeviceInfo& d, int64_t max_nv, bool paired, int want_vec, int stage_bytes,
+                bool tma_store, int* variant, int* block) {
+  for (const auto& group : kRowGroups) {
+    double best = -1.0;
+    for (int i : group) {
+      int b = 0;
+      if (i < 0 || !rowres_wanted(want_vec, i) || !rowres_block(max_nv, paired, i, &b)) continue;
+      int per_sm = 0;
+      CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(i, tma_store), b,
+                                                            2 * stage_bytes + cs::rowres_tail_bytes(2)));
+      const double regs = d.row_regs[tma_store ? 1 : 0][i];
+      const double score = (double)per_sm * (b / 32) * regs * std::sqrt(regs);
+      if (per_sm > 0 && score > best) {
+        best = score;
+        *variant = i;
+        *block = b;
+      }
+    }
+    if (best > 0) return CS_OK;
+  }
+  return CS_ERR_UNSUPPORTED;
 }
 
 // Row-resident kernel geometry; CS_ERR_UNSUPPORTED when a unit does not fit.
 int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tma_store,
                 LaunchPlan* lp) {
-  cs::UnitMap m = cs::make_unit_map(g, true);
-  int64_t max_nv = rowres_max_vectors(g, m);
-  int variant = -1, block = 0;
-  if (!rowres_shape(max_nv, m.n_pairs > 0, t.vec, &variant, &block)) {
-    // A pair may not fit where a single row still does.
-    m = cs::make_unit_map(g, false);
+  cs::UnitMap m{};
+  int64_t max_nv = 0;
+  int variant = -1, block = 0, stage_bytes = 0;
+  // Row pairs first; a pair may not fit where a single row still does.
+  for (bool paired : {true, false}) {
+    m = cs::make_unit_map(g, paired);
     max_nv = rowres_max_vectors(g, m);
-    rowres_shape(max_nv, false, t.vec, &variant, &block);
+    stage_bytes = (int)((max_nv * 16 + 127) / 128 * 128);
+    const int rc = rowres_pick(d, max_nv, m.n_pairs > 0, t.vec, stage_bytes, tma_store, &variant, &block);
+    if (rc == CS_OK) break;
+    if (rc != CS_ERR_UNSUPPORTED) return rc;
   }
   const int vec = variant >= 0 ? kRowVariants[variant].vec : 0;
   if (!vec) {
@@ -243,16 +292,26 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
                   (long long)max_nv);
     return CS_ERR_UNSUPPORTED;
   }
-  const int stage_bytes = (int)((max_nv * 16 + 127) / 128 * 128);
   int stages = t.stages ? t.stages : kDefaultStages;
   if (!t.stages) {
-    // Two stages once the SM's resident CTAs hold kRingBytesPerSm in their
-    // rings: measured on B200, a third stage then costs 7% (256 x 4096^2)
-    // to 48% (32768^2); below it (one CTA of 8192-wide rows) it gains 8%.
-    int per_sm2 = 0;
-    CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm2, rowres_kernel_ptr(variant, tma_store), block, 2 * stage_bytes + cs::rowres_tail_bytes(2)));
-    if ((int64_t)per_sm2 * 2 * stage_bytes >= kRingBytesPerSm) stages = 2;
+    // The ring depth that puts closest to kRingBytesPerSm of stages on each
+    // SM (all its resident CTAs together), at least two. Measured on B200
+    // over square widths 2048..32768: 64-80 KB per SM is best; a deeper ring
+    // costs up to 48% (32768^2 at 192 KB), a shallower one up to 12%.
+    double best = 1e30;
+    for (int s = 2; s <= kMaxAutoStages; ++s) {
+      const int64_t sm = (int64_t)s * stage_bytes + cs::rowres_tail_bytes(s);
+      if (sm > d.max_smem_optin) break;
+      int per_sm = 0;
+      CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(variant, tma_store),
+                                                            block, (size_t)sm));
+      if (per_sm < 1) break;
+      const double dist = std::fabs(std::log((double)per_sm * s * stage_bytes / (double)kRingBytesPerSm));
+      if (dist < best - 1e-9) {
+        best = dist;
+        stages = s;
+      }
+    }
   }
   while (stages > 1 && (int64_t)stages * stage_bytes + cs::rowres_tail_bytes(stages) > d.max_smem_optin)
     --stages;
@@ -582,8 +641,7 @@ int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols) {
     const cs::UnitMap m = cs::make_unit_map(g, paired);
     const int64_t max_nv = rowres_max_vectors(g, m);
     const int64_t stage = (max_nv * 16 + 127) / 128 * 128;
-    int vec = 0, block = 0;
-    if (rowres_shape(max_nv, m.n_pairs > 0, 0, &vec, &block) &&
+    if (rowres_shape(max_nv, m.n_pairs > 0, 0) &&
         2 * stage + cs::rowres_tail_bytes(2) <= 232448)
       return CS_KERNEL_PIPELINE;
   }

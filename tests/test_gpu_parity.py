@@ -245,6 +245,20 @@ def test_row_resident_tuning_variants(tuning):
             check(got, x, cols=cols, scale=0.125, what=f"{kernel} {tuning} {rows}x{cols}")
 
 
+@pytest.mark.parametrize("variant", range(7))
+def test_every_compiled_row_resident_variant(variant):
+    # Tuning vec 16 + i forces compiled variant i (V and register budget).
+    for rows, cols in [(2000, 2000), (6000, 6001)]:
+        x = cs.generate(2, 5, batch=1, rows=rows, cols=cols)[0]
+        for kernel in ("tma", "pipeline"):
+            try:
+                got = run(kernel, x, cols=cols, scale=0.0883883, tuning=(16 + variant, 0, -1, -1))
+            except cs.CausalSoftmaxError as e:
+                assert e.code == cs.ERR_CODE["UNSUPPORTED"], e
+                continue
+            check(got, x, cols=cols, scale=0.0883883, what=f"{kernel} variant {variant} {rows}x{cols}")
+
+
 def test_unpaired_fallback_when_a_pair_does_not_fit():
     # Forcing 2 vectors per thread caps a unit at 30 warps x 64 vectors: row
     # pairs of ~24000 columns do not fit, single rows (~1500 vectors) do, so
