@@ -88,7 +88,8 @@ class DeviceGuard {
   X(3, 2, 1024, 1)         \
   X(4, 4, 224, 4)          \
   X(5, 2, 352, 3)          \
-  X(6, 4, 384, 2)
+  X(6, 4, 384, 2)          \
+  X(7, 0, 1024, 1)
 
 struct RowVariant {
   int vec;
@@ -217,6 +218,13 @@ int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
 // variant cannot hold such a unit.
 bool rowres_block(int64_t max_nv, bool paired, int i, int* block) {
   const int v = kRowVariants[i].vec;
+  if (v == 0) {
+    // Shared-memory passes: about 4 vectors per lane and pass, 2..31 consumer warps.
+    const int64_t want = (max_nv + 127) / 128;
+    const int64_t w = want < 2 ? 2 : (want > 31 ? 31 : want);
+    *block = (int)(32 * (w + 1));
+    return true;
+  }
   const int64_t warps = (max_nv + 32 * v - 1) / (32 * v) + (paired ? 1 : 0) + 1;
   if (warps > 31 || 32 * warps > kRowVariants[i].maxt) return false;
   *block = (int)(32 * warps);
@@ -238,10 +246,13 @@ bool rowres_shape(int64_t max_nv, bool paired, int want_vec) {
   return false;
 }
 
-// Variant groups in order of preference: V = 4 first, then 8, then 2
-// (measured on B200 over square widths 1024..32768: V = 4 wins wherever it
-// fits; V = 8 only where it does not; V = 2 only below ~1500 columns).
-constexpr int kRowGroups[3][3] = {{4, 6, 2}, {0, 1, -1}, {5, 3, -1}};
+// Variant groups in order of preference: V = 4 first, then the
+// shared-memory passes (V = 0), then V = 8 and V = 2, which only a tuning
+// request reaches. Measured on B200 over square widths 1024..32768: V = 4
+// wins wherever it fits (up to ~12000 columns; 6108 GB/s at 12288 against
+// 6027 for V = 0); beyond, V = 0 beats V = 8 by 7-36% (16384^2: 5509 against
+// 4655 GB/s; 32768^2: 526 against 714 us).
+constexpr int kRowGroups[4][3] = {{4, 6, 2}, {7, -1, -1}, {0, 1, -1}, {5, 3, -1}};
 
 // Pick the variant for units of up to max_nv vectors. Within a group the
 // score is resident warps per SM x registers^1.5: more resident warps hide
@@ -287,25 +298,32 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
     if (rc != CS_ERR_UNSUPPORTED) return rc;
   }
   const int vec = variant >= 0 ? kRowVariants[variant].vec : 0;
-  if (!vec) {
+  if (variant < 0) {
     std::snprintf(t_detail, sizeof t_detail, "row-resident kernel: %lld vectors per unit do not fit",
                   (long long)max_nv);
     return CS_ERR_UNSUPPORTED;
   }
   int stages = t.stages ? t.stages : kDefaultStages;
-  if (!t.stages) {
+  if (!t.stages && vec == 0) {
+    // Shared-memory passes: two stages (measured best or within 4% from
+    // 4096 to 32768 columns; a third costs 10% at 32768^2).
+    stages = 2;
+  } else if (!t.stages) {
     // The ring depth that puts closest to kRingBytesPerSm of stages on each
-    // SM (all its resident CTAs together), at least two. Measured on B200
-    // over square widths 2048..32768: 64-80 KB per SM is best; a deeper ring
-    // costs up to 48% (32768^2 at 192 KB), a shallower one up to 12%.
+    // SM (all its resident CTAs together), at least two, without losing a
+    // resident CTA. Measured on B200 over square widths 2048..32768: 64-80 KB
+    // per SM is best; a deeper ring costs up to 48% (32768^2 at 192 KB), a
+    // shallower one up to 12%.
     double best = 1e30;
+    int per_sm2 = 0;
     for (int s = 2; s <= kMaxAutoStages; ++s) {
       const int64_t sm = (int64_t)s * stage_bytes + cs::rowres_tail_bytes(s);
       if (sm > d.max_smem_optin) break;
       int per_sm = 0;
       CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowres_kernel_ptr(variant, tma_store),
                                                             block, (size_t)sm));
-      if (per_sm < 1) break;
+      if (s == 2) per_sm2 = per_sm;
+      if (per_sm < 1 || per_sm < per_sm2) break;
       const double dist = std::fabs(std::log((double)per_sm * s * stage_bytes / (double)kRingBytesPerSm));
       if (dist < best - 1e-9) {
         best = dist;

@@ -54,8 +54,159 @@ __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
   return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
 }
 
-// V: 16-byte vectors per consumer lane; MAXT / MINB: launch bounds (CTA
-// size and resident CTAs per SM), which set the register budget.
+// Shared-memory-resident consumers (V == 0), for rows too long to hold in
+// registers: each unit's rows stay in their ring stage and every consumer
+// warp makes three passes over its contiguous chunk of one row -- the max,
+// the sum of exp2((x - m_w) * scale*log2 e), and after the one barrier of the
+// unit, p = exp2((x - M) * scale*log2 e) / S -- so a lane holds no row data
+// between passes and 31 consumer warps fit one SM. Warps are given to the two
+// rows of a pair in proportion to their lengths.
+template <bool kTmaStore>
+__device__ __forceinline__ void rowres_pass_consumers(const RowResParams& p, uint8_t* stage_base, float2* red,
+                                                      uint64_t* full, uint64_t* empty,
+                                                      volatile int* abort_flag, int warp, int lane, int W,
+                                                      int32_t first, int32_t n_mine) {
+  const Geometry& g = p.g;
+  const int S = p.stages;
+  const int32_t G = gridDim.x;
+  const int32_t upm = p.m.units_per_matrix;
+  const int32_t gq = G / upm, gr = G - (G / upm) * upm;
+  const int32_t pv = g.pitch >> 3;
+  const float sl = g.scale * kLog2e;
+  const float2 sl2 = make_float2(sl, sl);
+  const bool zero_scale = sl == 0.f;
+  int32_t b = first / upm, kk = first - (first / upm) * upm;
+  int s = 0;
+  uint32_t parity = 0;
+  for (int32_t k = 0; k < n_mine; ++k) {
+    int32_t ra, rb;
+    unit_rows(p.m, kk, ra, rb);
+    const int32_t va = valid_cols(g, ra);
+    const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
+    const int32_t na = (va + 7) >> 3, nb = (vb + 7) >> 3;
+    int32_t wa = W;
+    if (nb > 0) {
+      wa = (int32_t)(((int64_t)W * na + (na + nb) / 2) / (na + nb));
+      wa = wa < 1 ? 1 : (wa > W - 1 ? W - 1 : wa);
+    }
+    const bool row_a = warp < wa;
+    const int32_t w_first = row_a ? 0 : wa, w_count = row_a ? wa : W - wa;
+    const int32_t n_row = row_a ? na : nb;
+    const int32_t valid = row_a ? va : vb;
+    // This warp's chunk: whole groups of 32 vectors, so lane j takes every
+    // 32nd vector from c0 + j.
+    const int32_t groups = (n_row + 31) >> 5;
+    const int32_t per = (groups + w_count - 1) / w_count;
+    const int32_t gs = (warp - w_first) * per;
+    const int32_t c0 = (gs < groups ? gs : groups) * 32;
+    const int32_t c1e = c0 + per * 32;
+    const int32_t c1 = c1e < n_row ? c1e : n_row;
+
+    const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
+    if (!ok) {
+      *abort_flag = 1;
+      if (g.status) atomicOr(g.status, kStatusTimeout);
+    }
+    uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
+    constexpr uint32_t kNeg2 = kHalfNegInf | (kHalfNegInf << 16);
+    auto load = [&](int32_t v) {
+      uint4 r = *reinterpret_cast<const uint4*>(st + (size_t)v * 16);
+      const int32_t lim = valid - v * 8;
+      if (lim < 8) r = mask_tail_neg_inf(r, lim);
+      return r;
+    };
+    // Pass 1: the warp's max (packed halves, exact).
+    uint32_t hm = kNeg2;
+    if (ok)
+      for (int32_t v = c0 + lane; v < c1; v += 32) {
+        const uint4 r = load(v);
+        hm = h2_bits(__hmax2(bits_h2(hm), __hmax2(__hmax2(bits_h2(r.x), bits_h2(r.y)),
+                                                   __hmax2(bits_h2(r.z), bits_h2(r.w)))));
+      }
+    const __half2 hm2 = bits_h2(hm);
+    const float mw = redux_max(__half2float(__hmax(__low2half(hm2), __high2half(hm2))));
+    // Pass 2: the warp's sum relative to its own max.
+    float2 acc = make_float2(0.f, 0.f);
+    if (ok && mw > -INFINITY) {
+      const float2 nm2 = make_float2(-mw, -mw);
+      for (int32_t v = c0 + lane; v < c1; v += 32) {
+        const uint4 r = load(v);
+        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 e;
+          if (zero_scale) {
+            e.x = (w4[q] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
+            e.y = (w4[q] >> 16) == kHalfNegInf ? 0.f : 1.f;
+          } else {
+            const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[q])), nm2), sl2);
+            e = make_float2(ex2(d.x), ex2(d.y));
+          }
+          acc = __fadd2_rn(acc, e);
+        }
+      }
+    }
+    const float sw = warp_sum(acc.x + acc.y);
+    float2* rk = red + (k & 1) * 32;
+    if (lane == 0) rk[warp] = make_float2(mw, sw);
+    asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumer warps only
+    if (*abort_flag) break;
+
+    // Merge the row's warps: max M and sum S; then pass 3 writes exp2((x - M)*sl) / S.
+    const float2 ps = lane < w_count ? rk[w_first + lane] : make_float2(-INFINITY, 0.f);
+    const float M = redux_max(ps.x);
+    const float Ssum = warp_sum(ps.x > -INFINITY ? ps.y * ex2((ps.x - M) * sl) : 0.f);
+    const float rs = rcp_rn(Ssum);
+    const float2 rs2 = make_float2(rs, rs);
+    const float2 nM2 = make_float2(-M, -M);
+    uint16_t* out_row = g.out + (int64_t)b * g.batch_stride + (int64_t)(row_a ? ra : rb) * g.pitch;
+    for (int32_t v = c0 + lane; v < c1; v += 32) {
+      const uint4 r = load(v);
+      const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 e;
+        if (zero_scale) {
+          e.x = (w4[q] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
+          e.y = (w4[q] >> 16) == kHalfNegInf ? 0.f : 1.f;
+        } else {
+          const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[q])), nM2), sl2);
+          e = make_float2(ex2(d.x), ex2(d.y));
+        }
+        const float2 pr = __fmul2_rn(e, rs2);
+        o[q] = float2_to_half2_bits(pr.x, pr.y);
+      }
+      const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+      if (kTmaStore)
+        *reinterpret_cast<uint4*>(st + (size_t)v * 16) = ov;
+      else
+        *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = ov;
+    }
+    if (kTmaStore) fence_proxy_async_smem();  // outputs visible to the bulk-store engine
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage
+    if (!p.zero_tma && w_first == warp) {
+      // Masked columns and pitch padding by the row's first warp (no loads).
+      for (int32_t zi = n_row + lane; zi < pv; zi += 32)
+        *reinterpret_cast<uint4*>(out_row + (int64_t)zi * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    kk += gr;
+    b += gq;
+    if (kk >= upm) {
+      kk -= upm;
+      ++b;
+    }
+    if (++s == S) {
+      s = 0;
+      parity ^= 1u;
+    }
+  }
+}
+
+// V: 16-byte vectors per consumer lane (0: rows stay in shared memory, see
+// rowres_pass_consumers); MAXT / MINB: launch bounds (CTA size and resident
+// CTAs per SM), which set the register budget.
 template <int V, int MAXT, int MINB, bool kTmaStore>
 __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constant__ RowResParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -188,6 +339,10 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
   }
 
   // -------------------------------------------------------------- consumers
+  if constexpr (V == 0) {
+    rowres_pass_consumers<kTmaStore>(p, stage_base, red, full, empty, abort_flag, warp, lane, W, first,
+                                     n_mine);
+  } else {
   const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   const float2 sl2 = make_float2(sl, sl);
   constexpr int kSeg = 32 * V;  // vectors per warp segment
@@ -337,6 +492,7 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
       parity ^= 1u;
     }
   }
+  }  // V > 0
 }
 
 }  // namespace cs
