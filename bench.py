@@ -5,12 +5,13 @@
 
 Default workload (one step): the batched multi-head configuration, B=8 x H=32
 causal softmaxes of 4096 x 4096 FP16 scores (256 matrices, 8 GiB in, 8 GiB
-out), values half(N(0,1)*3) from seed 3, scale 1/sqrt(128), heads sharded
-evenly over the N ranks (one process per GPU, launched by torchrun for N > 1).
-The single-matrix workloads (c1 4096^2, c2a 1000x1037 pitch 1040, c2b 4096x32,
-c3 8192^2 stress, c5 32768^2) shard row blocks balanced by causal area
-(row_offset per rank). There is no collective on the data path: ranks meet
-only at the timing barriers.
+out), values half(N(0,1)*3) from seed 3, scale 1/sqrt(128). With N ranks (one
+process per GPU, launched by torchrun for N > 1) every rank runs its own batch
+of 256 independent heads (weak scaling: the job is N x 256 matrices). The
+single-matrix workloads (c1 4096^2, c2a 1000x1037 pitch 1040, c2b 4096x32, c3
+8192^2 stress, c5 32768^2) shard one matrix in row blocks balanced by causal
+area (row_offset per rank; strong scaling). There is no collective on the data
+path: ranks meet only at the timing barriers.
 
 value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
          write 2*M*N per matrix) / step time, in GB/s; step time is the max
@@ -20,6 +21,8 @@ value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
 e2e    = the same metric through the host-buffer API (cs_session_softmax_host):
          pinned host input -> device -> kernel -> pinned host output per step,
          host wall clock around the blocking call, max over ranks.
+graph  = single-matrix workloads only: the same launches captured k at a time
+         in a CUDA graph, device time per launch (labelled; not the value).
 roofline  = the single kernel's per-launch algorithmic bytes / per-launch time
             against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
 cpu_baseline = the reference CPU path (C restatement of
@@ -53,7 +56,7 @@ WORKLOADS = {
     "c4": dict(config=4, seed=3, matrices=256, rows=4096, cols=4096, pitch=4096, scale=INV_SQRT128,
                shard="heads", values="half(N(0,1)*3)",
                desc="batched multi-head causal softmax, B=8 H=32 L=4096: 256 matrices of "
-                    "4096x4096 FP16 scores, heads sharded over ranks"),
+                    "4096x4096 FP16 scores per rank"),
     "c1": dict(config=1, seed=0, matrices=1, rows=4096, cols=4096, pitch=4096, scale=INV_SQRT128,
                shard="rows", values="half(N(0,1)*4)",
                desc="single 4096x4096 causal softmax, row blocks sharded over ranks"),
@@ -243,8 +246,8 @@ def run_reference(args, w: dict) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "io_dtype": "f16",
-        "data": "synthetic",
+        "scaling": "weak" if w["shard"] == "heads" else "strong", "vs_baseline": None,
+        "dtype": "f32", "io_dtype": "f16", "data": "synthetic",
         "config": {"workload": w["desc"], "rows": rows, "cols": cols, "pitch": pitch,
                    "values": w["values"], "seed": w["seed"], "scale": w["scale"],
                    "sample_rows_per_step": n, "sample_first_row": off},
@@ -269,6 +272,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="skip the CUDA-graph timing of the single-matrix workloads")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--tuning", default="",
                     help="vec,stages,l2_hint,zero_fill_tma (0/-1 = automatic)")
@@ -310,13 +315,17 @@ def main() -> int:
     rows_full, cols, pitch = w["rows"], w["cols"], w["pitch"]
     scale = f32(w["scale"])
     if w["shard"] == "heads":
-        if w["matrices"] % world:
-            raise SystemExit(f"{w['matrices']} heads must split evenly over {world} ranks")
-        n_local, first_b = w["matrices"] // world, rank * (w["matrices"] // world)
+        # Weak scaling: every rank runs its own batch of independent heads
+        # (matrices rank*M .. rank*M + M - 1 of the seeded stream); there is
+        # no exchange between ranks on this path.
+        n_local, first_b = w["matrices"], rank * w["matrices"]
         r0, r1 = 0, rows_full
+        scaling, job_matrices = "weak", w["matrices"] * world
     else:
+        # Strong scaling: the rows of one matrix, in blocks of equal causal cost.
         n_local, first_b = w["matrices"], 0
         r0, r1 = row_blocks(rows_full, cols, world)[rank]
+        scaling, job_matrices = "strong", w["matrices"]
     rows = r1 - r0
 
     # This rank's input on the host (pinned) and on the device; rotate copies
@@ -379,7 +388,7 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
     alg_local = info["algorithmic_bytes"]
-    alg_total = cs.roofline_bytes(rows_full, cols) * w["matrices"]
+    alg_total = cs.roofline_bytes(rows_full, cols) * job_matrices
     value = alg_total / (ms_step / 1e3) / 1e9
 
     peak, peak_kind = measured_peak()
@@ -393,6 +402,42 @@ def main() -> int:
                           f"smem={info['smem_bytes']} stages={info['stages']} "
                           f"vec={info['vec_per_thread']}"}
     clk = clocks.summary()
+
+    # Single-matrix workloads: the same launches captured in one CUDA graph
+    # (k launches per replay, device time / k), which removes the host's
+    # per-launch cost; reported beside the stream-launched value, not in it.
+    graph = None
+    if w["matrices"] == 1 and not args.no_graph:
+        k = max(1, min(args.steps, 100))
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side, capture_error_mode="thread_local"):
+            for i in range(k):
+                plans[i % n_rot].launch(args.kernel, scale)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = max(3, 2000 // k)
+        ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        ga.record()
+        for _ in range(reps):
+            g.replay()
+        gb.record()
+        torch.cuda.synchronize()
+        gt = torch.tensor([ga.elapsed_time(gb) / (reps * k)], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        g_ms = float(gt.item())
+        for p in plans:
+            rc, st = p.status()
+            if rc != 0:
+                raise SystemExit(f"device status {st} after the graph replays")
+        graph = {"value": round(alg_total / (g_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                 "us_per_launch": round(g_ms * 1e3, 3), "launches_per_graph": k, "replays": reps,
+                 "timing": "CUDA graph of k launches replayed R times, device time / (R k), max over ranks"}
+        del g
     for p in plans:
         p.close()
 
@@ -423,7 +468,7 @@ def main() -> int:
         if world > 1:
             dist.all_reduce(e_step, op=dist.ReduceOp.MAX)
         e_s = float(e_step.item())
-        dense_bytes = w["matrices"] * rows_full * cols * 2
+        dense_bytes = job_matrices * rows_full * cols * 2  # all ranks
         e2e = {"value": round(alg_total / e_s / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": dense_bytes, "d2h_bytes_per_step": dense_bytes,
                "ms_per_step": round(e_s * 1e3, 3),
@@ -439,15 +484,16 @@ def main() -> int:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "io_dtype": "f16", "data": "synthetic",
-            "config": {"workload": w["desc"], "name": args.workload, "matrices": w["matrices"],
+            "config": {"workload": w["desc"], "name": args.workload, "matrices": job_matrices,
+                       "matrices_per_rank": n_local,
                        "rows": rows_full, "cols": cols, "pitch": pitch, "values": w["values"],
                        "seed": w["seed"], "scale": w["scale"], "kernel": info["kernel_name"],
                        "l2": l2},
-            "matrices_per_s": round(w["matrices"] / (ms_step / 1e3), 2),
+            "matrices_per_s": round(job_matrices / (ms_step / 1e3), 2),
             "roofline_pct": round(100.0 * value / (peak * world), 2),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "graph": graph,
             "gpu_launches": args.steps * world, "gpu_launches_per_rank": args.steps,
         }
         print(json.dumps(line), flush=True)

@@ -184,6 +184,9 @@ def check(rc: int, where: str) -> None:
 
 def kernel_id(kernel) -> int:
     if isinstance(kernel, str):
+        k = KERNELS.get(kernel)  # the canonical names, without a call into the library
+        if k is not None:
+            return k
         k = lib().cs_kernel_parse(kernel.encode())
         if k < 0:
             raise CausalSoftmaxError(k, f"kernel {kernel!r}")

@@ -421,7 +421,7 @@ int plan_baseline(const DeviceInfo& d, const Geometry& g, LaunchPlan* lp) {
 }
 
 // Resolve AUTO for a concrete geometry and build the launch plan.
-int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+int make_plan_uncached(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
   if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
   switch (kernel) {
     case CS_KERNEL_BASELINE: return plan_baseline(d, g, lp);
@@ -442,6 +442,50 @@ int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& 
   const int rc = plan_rowres(d, g, t, true, lp);
   if (rc != CS_ERR_UNSUPPORTED) return rc;
   return plan_online(d, g, t, lp);
+}
+
+// Planning asks the occupancy calculator about several variants and ring
+// depths (tens of microseconds of host time), while a launch of a small
+// matrix takes a few microseconds on the GPU. Plans therefore depend only on
+// the shape, tuning and device, and are kept per host thread: a repeat
+// launch of the same shape costs a lookup plus the geometry copy.
+struct PlanKey {
+  const DeviceInfo* dev;
+  int kernel;
+  Tuning t;
+  int64_t batch, batch_stride;
+  int32_t rows, cols, pitch, row_offset;
+  bool operator==(const PlanKey& o) const {
+    return dev == o.dev && kernel == o.kernel && t.vec == o.t.vec && t.stages == o.t.stages &&
+           t.hint == o.t.hint && t.zero_tma == o.t.zero_tma && batch == o.batch &&
+           batch_stride == o.batch_stride && rows == o.rows && cols == o.cols && pitch == o.pitch &&
+           row_offset == o.row_offset;
+  }
+};
+constexpr int kPlanCacheSize = 16;
+thread_local PlanKey t_plan_keys[kPlanCacheSize];
+thread_local LaunchPlan t_plans[kPlanCacheSize];
+thread_local int t_plan_count = 0, t_plan_next = 0;
+
+int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+  const PlanKey key{&d, kernel, t, g.batch, g.batch_stride, g.rows, g.cols, g.pitch, g.row_offset};
+  for (int i = 0; i < t_plan_count; ++i) {
+    if (t_plan_keys[i] == key) {
+      *lp = t_plans[i];
+      lp->rr.g = g;  // pointers, scale, status word, flags and timeout of this call
+      lp->on.g = g;
+      lp->nr.g = g;
+      lp->bl.g = g;
+      return CS_OK;
+    }
+  }
+  const int rc = make_plan_uncached(d, kernel, g, t, lp);
+  if (rc) return rc;
+  t_plan_keys[t_plan_next] = key;
+  t_plans[t_plan_next] = *lp;
+  t_plan_next = (t_plan_next + 1) % kPlanCacheSize;
+  if (t_plan_count < kPlanCacheSize) ++t_plan_count;
+  return CS_OK;
 }
 
 int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
