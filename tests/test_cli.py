@@ -1,7 +1,8 @@
 """The csm CLI (mirror of gpu/src/driver.rs:386-428 over the C ABI).
 
 CPU: flag parsing and validation messages (host/src/lib.rs:103-182).
-GPU: --probe, the --gpu-tests self-check matrix, and a --bench line.
+GPU: --probe, the --gpu-tests self-check matrix, a --bench line, and the
+--bench-suite categories of gpu/src/driver/bench.rs:139-369.
 """
 import os
 import subprocess
@@ -47,3 +48,23 @@ def test_cli_on_gpu():
     assert r.returncode == 0 and r.stdout.startswith("PASS"), r.stdout + r.stderr
     r = run("--bench", "--rows", "2048", "--cols", "2048", "--iterations", "5", "--warmup", "2")
     assert r.returncode == 0 and r.stdout.count("BENCH kernel=") == 4, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_bench_suite_categories():
+    r = run("--bench-suite", "--rows", "2048", "--cols", "2048", "--iterations", "3", "--warmup", "1")
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr
+    lines = r.stdout.splitlines()
+    assert lines[0].startswith("BENCH hardware=")
+    cats = {}
+    for ln in lines[1:]:
+        assert ln.startswith("BENCH category="), ln
+        cat = ln.split()[1].split("=")[1]
+        cats[cat] = cats.get(cat, 0) + 1
+    # 12 shapes x supported kernels (all 5 up to 32 columns, else 4); 4 queue
+    # depths x kernels; 3 transfer stages; 1 device copy; 6 patterns x 4 scales
+    # x kernels; 1/2/4/8 streams.
+    assert cats["shape"] == 3 * 5 + 9 * 4 and cats["queue"] == 4 * 4, cats
+    assert cats["transfer"] == 3 and cats["device_copy"] == 1, cats
+    assert cats["pattern"] == 6 * 4 * 4 and cats["concurrency"] == 4, cats
+    assert all("median_ms=" in ln or "batch_p50_ms=" in ln for ln in lines[1:])
