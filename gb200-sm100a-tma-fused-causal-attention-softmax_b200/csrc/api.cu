@@ -488,16 +488,37 @@ int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& 
   return CS_OK;
 }
 
+// Every library kernel is launched with programmatic stream serialization:
+// its CTAs may start (and set up shared memory and barriers) while the
+// previous kernel in the stream finishes; the kernel waits for that kernel's
+// completion (pdl_wait) before touching global memory.
+template <typename Params>
+cudaError_t launch_pdl(void (*kernel)(Params), int grid, int block, int smem, cudaStream_t stream,
+                       const Params& p) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
   switch (lp.kernel) {
     case CS_KERNEL_TMA:
     case CS_KERNEL_PIPELINE: {
       const bool ts = lp.kernel == CS_KERNEL_PIPELINE;
       switch (lp.variant) {
-#define CS_ROW_LAUNCH(i, v, t, b)                                                          \
-  case i:                                                                                  \
-    if (ts) cs::rowres_kernel<v, t, b, true><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr); \
-    else cs::rowres_kernel<v, t, b, false><<<lp.grid, lp.block, lp.smem, stream>>>(lp.rr);   \
+#define CS_ROW_LAUNCH(i, v, t, b)                                                                   \
+  case i:                                                                                           \
+    e = ts ? launch_pdl(&cs::rowres_kernel<v, t, b, true>, lp.grid, lp.block, lp.smem, stream, lp.rr) \
+           : launch_pdl(&cs::rowres_kernel<v, t, b, false>, lp.grid, lp.block, lp.smem, stream, lp.rr); \
     break;
         CS_ROW_VARIANTS(CS_ROW_LAUNCH)
 #undef CS_ROW_LAUNCH
@@ -506,25 +527,28 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
       break;
     }
     case CS_KERNEL_ONLINE:
-      cs::online_kernel<<<lp.grid, lp.block, lp.smem, stream>>>(lp.on);
+      e = launch_pdl(&cs::online_kernel, lp.grid, lp.block, lp.smem, stream, lp.on);
       break;
-    case CS_KERNEL_WARP:
+    case CS_KERNEL_WARP: {
+      void (*k)(cs::NarrowParams) = nullptr;
       switch (lp.narrow_lanes) {
-        case 1: cs::narrow_kernel<1><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
-        case 2: cs::narrow_kernel<2><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
-        case 4: cs::narrow_kernel<4><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
-        case 8: cs::narrow_kernel<8><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
-        case 16: cs::narrow_kernel<16><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
-        default: cs::narrow_kernel<32><<<lp.grid, lp.block, 0, stream>>>(lp.nr); break;
+        case 1: k = &cs::narrow_kernel<1>; break;
+        case 2: k = &cs::narrow_kernel<2>; break;
+        case 4: k = &cs::narrow_kernel<4>; break;
+        case 8: k = &cs::narrow_kernel<8>; break;
+        case 16: k = &cs::narrow_kernel<16>; break;
+        default: k = &cs::narrow_kernel<32>; break;
       }
+      e = launch_pdl(k, lp.grid, lp.block, 0, stream, lp.nr);
       break;
+    }
     case CS_KERNEL_BASELINE:
-      cs::baseline_kernel<<<lp.grid, lp.block, 0, stream>>>(lp.bl);
+      e = launch_pdl(&cs::baseline_kernel, lp.grid, lp.block, 0, stream, lp.bl);
       break;
     default:
       return CS_ERR_BAD_KERNEL;
   }
-  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return CS_OK;
 }

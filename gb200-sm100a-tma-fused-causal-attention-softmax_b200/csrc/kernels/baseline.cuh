@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(256) baseline_kernel(const __grid_constant__ B
   const Geometry& g = p.g;
   const int32_t pv = g.pitch >> 3;
   const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
+  pdl_trigger();
+  pdl_wait();
   for (int64_t flat = blockIdx.x; flat < p.total_rows; flat += gridDim.x) {
     const int64_t b = flat / g.rows;
     const int32_t i = (int32_t)(flat - b * g.rows);

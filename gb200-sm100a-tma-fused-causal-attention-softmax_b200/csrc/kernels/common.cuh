@@ -30,6 +30,16 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Programmatic dependent launch. The library launches its kernels with the
+// programmatic-stream-serialization attribute, so a kernel's CTAs may start
+// while the previous kernel in the stream is still running. pdl_wait blocks
+// until that kernel has completed and its memory is visible (every kernel
+// calls it before its first global load or store); pdl_trigger lets the next
+// kernel's CTAs start their own set-up early. Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
                : "memory");

@@ -30,6 +30,8 @@ __global__ void __launch_bounds__(256) narrow_kernel(const __grid_constant__ Nar
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int32_t pv = g.pitch >> 3;
   const float sl = g.scale * kLog2e;
+  pdl_trigger();
+  pdl_wait();
 
   for (int64_t base = warp_id * R; base < p.total_rows; base += n_warps * R) {
     const int64_t flat = base + lane / L;

@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // inputs written, outputs read by the previous kernel: done
 
   // Row j of this CTA -> element offset of its first column and valid count.
   auto row_of = [&](int64_t j, int64_t& off, int32_t& valid) {

@@ -244,6 +244,8 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // inputs written, outputs read by the previous kernel: done
 
   if (warp == W) {
     // ------------------------------------------------------------ producer
