@@ -23,6 +23,8 @@ struct Geometry {
   int32_t row_offset;    // absolute causal row of local row 0
   float scale;
   uint32_t* status;      // device status word (atomicOr of kStatus* bits)
+  uint32_t* sched;       // row-resident kernel: {claim, done} counters of the dynamic
+                         // schedule, zero between launches; nullptr: static schedule
   uint64_t timeout_ns;   // bound on every mbarrier wait
   uint32_t flags;        // debug flags (kFlag*), 0 in production launches
 };

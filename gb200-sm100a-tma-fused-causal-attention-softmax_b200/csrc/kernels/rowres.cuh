@@ -49,9 +49,10 @@ struct RowResParams {
 };
 
 // Shared memory after the stages: zero buffer, 2 x 32 float2 (max, sum)
-// partials, full and empty mbarriers per stage, abort flag.
+// partials, full and empty mbarriers per stage, abort flag, and the unit each
+// stage holds (-1: no more units).
 __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
-  return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
+  return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16 + ((4 * stages + 15) / 16) * 16;
 }
 
 // Shared-memory-resident consumers (V == 0), for rows too long to hold in
@@ -64,21 +65,27 @@ __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
 template <bool kTmaStore>
 __device__ __forceinline__ void rowres_pass_consumers(const RowResParams& p, uint8_t* stage_base, float2* red,
                                                       uint64_t* full, uint64_t* empty,
-                                                      volatile int* abort_flag, int warp, int lane, int W,
-                                                      int32_t first, int32_t n_mine) {
+                                                      volatile int* abort_flag, const volatile int32_t* unit_id,
+                                                      int warp, int lane, int W) {
   const Geometry& g = p.g;
   const int S = p.stages;
-  const int32_t G = gridDim.x;
   const int32_t upm = p.m.units_per_matrix;
-  const int32_t gq = G / upm, gr = G - (G / upm) * upm;
   const int32_t pv = g.pitch >> 3;
   const float sl = g.scale * kLog2e;
   const float2 sl2 = make_float2(sl, sl);
   const bool zero_scale = sl == 0.f;
-  int32_t b = first / upm, kk = first - (first / upm) * upm;
   int s = 0;
   uint32_t parity = 0;
-  for (int32_t k = 0; k < n_mine; ++k) {
+  for (int32_t k = 0;; ++k) {
+    // The producer names each stage's unit (possibly claimed at run time).
+    const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
+    if (!ok) {
+      *abort_flag = 1;
+      if (g.status) atomicOr(g.status, kStatusTimeout);
+    }
+    const int32_t u = ok ? unit_id[s] : 0;
+    if (u < 0) break;
+    const int32_t b = u / upm, kk = u - (u / upm) * upm;
     int32_t ra, rb;
     unit_rows(p.m, kk, ra, rb);
     const int32_t va = valid_cols(g, ra);
@@ -101,12 +108,6 @@ __device__ __forceinline__ void rowres_pass_consumers(const RowResParams& p, uin
     const int32_t c0 = (gs < groups ? gs : groups) * 32;
     const int32_t c1e = c0 + per * 32;
     const int32_t c1 = c1e < n_row ? c1e : n_row;
-
-    const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
-    if (!ok) {
-      *abort_flag = 1;
-      if (g.status) atomicOr(g.status, kStatusTimeout);
-    }
     uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)(row_a ? 0 : na) * 16;
     constexpr uint32_t kNeg2 = kHalfNegInf | (kHalfNegInf << 16);
     auto load = [&](int32_t v) {
@@ -191,12 +192,6 @@ __device__ __forceinline__ void rowres_pass_consumers(const RowResParams& p, uin
       for (int32_t zi = n_row + lane; zi < pv; zi += 32)
         *reinterpret_cast<uint4*>(out_row + (int64_t)zi * 8) = make_uint4(0u, 0u, 0u, 0u);
     }
-    kk += gr;
-    b += gq;
-    if (kk >= upm) {
-      kk -= upm;
-      ++b;
-    }
     if (++s == S) {
       s = 0;
       parity ^= 1u;
@@ -220,9 +215,16 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 64);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  volatile int32_t* unit_id = reinterpret_cast<volatile int32_t*>(empty + S) + 4;
 
-  // Units advance by G per step; (matrix, unit) cursors are stepped
-  // incrementally. The host splits launches so that total_units < 2^30.
+  // Schedule: CTA c takes units c, c + G, ..., c + (S-1) G; after those,
+  // either the static sequence continues (c + S G, ...) or, with a schedule
+  // counter (g.sched, set for the shared-memory consumers only), the producer
+  // claims units from S G upwards one at a time, so CTAs that run ahead take
+  // more. The producer names each stage's unit in unit_id and marks the end
+  // with -1; the register-resident consumers follow the static sequence with
+  // their own cursor, so a unit's geometry is ready before its data arrives.
+  // The host splits launches so that total_units < 2^30.
   const int32_t G = gridDim.x;
   const int32_t first = blockIdx.x;
   const int32_t total = (int32_t)p.m.total_units;
@@ -251,7 +253,6 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
     // ------------------------------------------------------------ producer
     if (lane != 0 || skip_loads) return;
     const uint64_t policy = p.l2_hint ? policy_evict_first() : 0ull;
-    int32_t b = first / upm, kk = first - (first / upm) * upm;  // unit cursor
     // kTmaStore: the output of the unit that last used a stage is stored
     // from it before the stage is refilled.
     auto store_unit = [&](int32_t ub, int32_t uk, int s) {
@@ -266,84 +267,194 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
       bulk_commit();
     };
     int32_t sb[24], sk[24];  // unit held by each stage (kTmaStore)
-    bool aborted = false;
-    int32_t issued = 0;
-    for (int32_t k = 0; k < n_mine; ++k) {
-      const int s = k % S;
-      if (k >= S) {
-        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
-          aborted = true;
-          break;
-        }
-        if (kTmaStore) {
-          store_unit(sb[s], sk[s], s);
-          bulk_wait_read_all();  // the stage is read out before it is refilled
-        }
-      }
-      int32_t ra, rb;
-      unit_rows(p.m, kk, ra, rb);
-      const int32_t va = valid_cols(g, ra);
-      const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
-      const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
-      uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
-      const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
-      mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
-      if (p.l2_hint) {
-        bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
-        if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
-      } else {
-        bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
-        if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
-      }
-      ++issued;
-      if (p.zero_tma) {
-        uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
-        for (int r = 0; r < 2; ++r) {
-          const int32_t row = r == 0 ? ra : rb;
-          if (row < 0) break;
-          uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
-          uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
-          while (left) {
-            const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
-            bulk_s2g(z, zero_buf, n);
-            z += n;
-            left -= n;
+    if constexpr (V == 0) {
+      // Shared-memory consumers read each stage's unit from unit_id; units
+      // past the first S per CTA may be claimed at run time (g.sched).
+      bool aborted = false;
+      int32_t issued = 0;
+      // The unit of the next iteration: a static index, or a claim issued after
+      // this iteration's copies (its L2 round trip overlaps them).
+      int64_t next = first;
+      int32_t k = 0;
+      for (;; ++k) {
+        const int s = k % S;
+        if (k >= S) {
+          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
+            aborted = true;
+            *abort_flag = 1;
+            if (g.status) atomicOr(g.status, kStatusTimeout);
+            break;
+          }
+          if (kTmaStore) {
+            store_unit(sb[s], sk[s], s);
+            bulk_wait_read_all();  // the stage is read out before it is refilled
           }
         }
-        bulk_commit();
-        bulk_wait_read_16();
+        if (next >= total) {
+          unit_id[s] = -1;  // consumers that read unit ids stop here
+          mbar_arrive(&full[s]);
+          break;
+        }
+        const int32_t u = (int32_t)next;
+        unit_id[s] = u;
+        const int32_t b = u / upm, kk = u - (u / upm) * upm;
+        int32_t ra, rb;
+        unit_rows(p.m, kk, ra, rb);
+        const int32_t va = valid_cols(g, ra);
+        const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
+        const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
+        uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+        const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
+        mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
+        if (p.l2_hint) {
+          bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
+          if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
+        } else {
+          bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
+          if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
+        }
+        ++issued;
+        if (p.zero_tma) {
+          uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
+          for (int r = 0; r < 2; ++r) {
+            const int32_t row = r == 0 ? ra : rb;
+            if (row < 0) break;
+            uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
+            uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
+            while (left) {
+              const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
+              bulk_s2g(z, zero_buf, n);
+              z += n;
+              left -= n;
+            }
+          }
+          bulk_commit();
+          bulk_wait_read_16();
+        }
+        if (kTmaStore) {
+          sb[s] = b;
+          sk[s] = kk;
+        }
+        if (k + 1 < S || g.sched == nullptr)
+          next = (int64_t)first + (int64_t)(k + 1) * G;
+        else
+          next = (int64_t)S * G + atomicAdd(&g.sched[0], 1u);
       }
-      if (kTmaStore) {
-        sb[s] = b;
-        sk[s] = kk;
+      if (kTmaStore && !aborted) {
+        // Outputs of the units still held by the other stages (iteration k
+        // stored the one before it in its own stage).
+        for (int32_t j = k + 1; j < k + S; ++j) {
+          if (j - S < 0) continue;
+          const int s = j % S;
+          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((j / S) - 1) & 1), g.timeout_ns)) {
+            if (g.status) atomicOr(g.status, kStatusTimeout);
+            break;
+          }
+          store_unit(sb[s], sk[s], s);
+        }
       }
-      kk += gr;
-      b += gq;
-      if (kk >= upm) {
-        kk -= upm;
-        ++b;
+      if (g.sched != nullptr) {
+        // The last CTA to finish claiming resets the counters for the next launch.
+        __threadfence();
+        if (atomicAdd(&g.sched[1], 1u) == (uint32_t)G - 1) {
+          atomicExch(&g.sched[0], 0u);
+          atomicExch(&g.sched[1], 0u);
+        }
       }
-    }
-    if (kTmaStore && !aborted) {
-      // Outputs of the last min(S, n_mine) units.
-      for (int32_t k = n_mine; k < n_mine + S && k - S < n_mine; ++k) {
-        if (k < S) continue;
+      bulk_wait_all();
+      // After an abort: copies this warp issued that no consumer waited for.
+      // (Without one, every copy was consumed, and the stage that received the
+      // end mark has completed one more phase, so its parity no longer tells.)
+      if (aborted)
+        for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
+          (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+    } else {
+      // Register-resident consumers follow the static schedule with their own
+      // cursor; this producer steps the same cursor.
+      int32_t b = first / upm, kk = first - (first / upm) * upm;
+      bool aborted = false;
+      int32_t issued = 0;
+      for (int32_t k = 0; k < n_mine; ++k) {
         const int s = k % S;
-        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) break;
-        store_unit(sb[s], sk[s], s);
+        if (k >= S) {
+          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
+            aborted = true;
+            *abort_flag = 1;
+            if (g.status) atomicOr(g.status, kStatusTimeout);
+            break;
+          }
+          if (kTmaStore) {
+            store_unit(sb[s], sk[s], s);
+            bulk_wait_read_all();  // the stage is read out before it is refilled
+          }
+        }
+        int32_t ra, rb;
+        unit_rows(p.m, kk, ra, rb);
+        const int32_t va = valid_cols(g, ra);
+        const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
+        const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
+        uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+        const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
+        mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
+        if (p.l2_hint) {
+          bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
+          if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
+        } else {
+          bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
+          if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
+        }
+        ++issued;
+        if (p.zero_tma) {
+          uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
+          for (int r = 0; r < 2; ++r) {
+            const int32_t row = r == 0 ? ra : rb;
+            if (row < 0) break;
+            uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
+            uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
+            while (left) {
+              const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
+              bulk_s2g(z, zero_buf, n);
+              z += n;
+              left -= n;
+            }
+          }
+          bulk_commit();
+          bulk_wait_read_16();
+        }
+        if (kTmaStore) {
+          sb[s] = b;
+          sk[s] = kk;
+        }
+        kk += gr;
+        b += gq;
+        if (kk >= upm) {
+          kk -= upm;
+          ++b;
+        }
       }
+      if (kTmaStore && !aborted) {
+        // Outputs of the last min(S, n_mine) units.
+        for (int32_t k = n_mine; k < n_mine + S && k - S < n_mine; ++k) {
+          if (k < S) continue;
+          const int s = k % S;
+          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
+            if (g.status) atomicOr(g.status, kStatusTimeout);
+            break;
+          }
+          store_unit(sb[s], sk[s], s);
+        }
+      }
+      bulk_wait_all();
+      // Copies this warp issued that no consumer waited for (after an abort).
+      for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
+        (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
     }
-    bulk_wait_all();
-    // Copies this warp issued that no consumer waited for (after an abort).
-    for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
-      (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
     return;
   }
 
   // -------------------------------------------------------------- consumers
   if constexpr (V == 0) {
-    rowres_pass_consumers<kTmaStore>(p, stage_base, red, full, empty, abort_flag, warp, lane, W, first,
-                                     n_mine);
+    rowres_pass_consumers<kTmaStore>(p, stage_base, red, full, empty, abort_flag, unit_id, warp, lane, W);
   } else {
   const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   const float2 sl2 = make_float2(sl, sl);

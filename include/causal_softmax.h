@@ -152,7 +152,9 @@ int cs_plan_create(cs_plan **plan, int device, const void *d_in, void *d_out, in
 
 /* Enqueue the softmax on `stream` (replaces Session::launch_on,
  * gpu/src/driver.rs:108-211). Asynchronous: no host synchronisation and no
- * allocation. Errors: argument errors as cs_validate, CS_ERR_WARP_COLS,
+ * allocation. Launches of one plan must not overlap on the GPU (issue them
+ * on one stream, or order them with events): they share the plan's output
+ * and the work-schedule counters in its device word block. Errors: argument errors as cs_validate, CS_ERR_WARP_COLS,
  * CS_ERR_UNSUPPORTED, CS_ERR_CUDA. */
 int cs_plan_launch(cs_plan *plan, int kernel, float scale, void *stream);
 

@@ -261,6 +261,31 @@ def test_every_compiled_row_resident_variant(variant):
             check(got, x, cols=cols, scale=0.0883883, what=f"{kernel} variant {variant} {rows}x{cols}")
 
 
+@pytest.mark.parametrize("cols", [2048, 20000])
+def test_repeated_launches_are_fast_and_exact(cols):
+    # 100 back-to-back launches of one plan finish quickly (no launch waits
+    # out a bounded wait; the dynamic schedule's counters are reset by every
+    # launch), and the last output is still exact. 20000 columns select the
+    # shared-memory variant, which claims its units dynamically.
+    rows = 2048 if cols == 2048 else 600
+    x = cs.generate(1, 7, batch=1, rows=rows, cols=cols)[0]
+    d_in = to_dev(x)
+    for kernel in ("tma", "pipeline"):
+        d_out = sentinel_like(d_in)
+        with cs.Plan.for_tensors(d_in, d_out, cols=cols) as plan:
+            plan.launch(kernel, 0.125)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(100):
+                plan.launch(kernel, 0.125)
+            b.record()
+            torch.cuda.synchronize()
+            assert plan.status() == (0, 0)
+            assert a.elapsed_time(b) < 500.0, (kernel, a.elapsed_time(b))
+        check(from_dev(d_out), x, cols=cols, scale=0.125, what=f"repeated {kernel} {rows}x{cols}")
+
+
 def test_unpaired_fallback_when_a_pair_does_not_fit():
     # Forcing 2 vectors per thread caps a unit at 30 warps x 64 vectors: row
     # pairs of ~24000 columns do not fit, single rows (~1500 vectors) do, so
