@@ -21,6 +21,9 @@ value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
 e2e    = the same metric through the host-buffer API (cs_session_softmax_host):
          pinned host input -> device -> kernel -> pinned host output per step,
          host wall clock around the blocking call, max over ranks.
+gather = N > 1 only: every rank's output shard sent to rank 0 over NCCL
+         (NVLink), after the timed region; GB/s of the bytes rank 0 receives.
+         For row blocks rank 0 assembles the matrix and checks its row sums.
 graph  = single-matrix workloads only: the same launches captured k at a time
          in a CUDA graph, device time per launch (labelled; not the value).
 roofline  = the single kernel's per-launch algorithmic bytes / per-launch time
@@ -272,6 +275,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="N > 1: skip the separately reported gather of all outputs to rank 0")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the CUDA-graph timing of the single-matrix workloads")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -441,6 +446,54 @@ def main() -> int:
     for p in plans:
         p.close()
 
+    # Optional final gather (N > 1): every rank's output shard to rank 0 over
+    # NCCL, outside the timed region and reported on its own. For row blocks
+    # rank 0 assembles the whole matrix and checks its row sums.
+    gather = None
+    if world > 1 and not args.no_gather:
+        shard = d_out[0].reshape(-1)  # fp16 (NCCL moves the bits unchanged)
+        counts = torch.tensor([shard.numel()], dtype=torch.int64, device="cuda")
+        all_counts = [torch.zeros_like(counts) for _ in range(world)]
+        dist.all_gather(all_counts, counts)
+        sizes = [int(c.item()) for c in all_counts]
+        recv = None
+        if rank == 0:
+            recv = torch.empty(sum(sizes), dtype=torch.float16, device="cuda")
+            recv[:sizes[0]].copy_(shard)
+        def gather_once():
+            if rank == 0:
+                ops, off = [], sizes[0]
+                for r in range(1, world):
+                    ops.append(dist.P2POp(dist.irecv, recv[off:off + sizes[r]], r))
+                    off += sizes[r]
+            else:
+                ops = [dist.P2POp(dist.isend, shard, 0)]
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+
+        gather_once()  # untimed: NCCL sets up its peer connections on first use
+        ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        ga.record()
+        gather_once()
+        gb.record()
+        torch.cuda.synchronize()
+        gt = torch.tensor([ga.elapsed_time(gb)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        moved = 2 * (sum(sizes) - sizes[0])
+        gather = {"value": round(moved / (float(gt.item()) / 1e3) / 1e9, 2), "unit": "GB/s",
+                  "bytes": moved, "ms": round(float(gt.item()), 3),
+                  "timing": "NCCL send/recv of every rank's output to rank 0, device time, max over ranks"}
+        if rank == 0 and w["shard"] == "rows":
+            full = recv.reshape(rows_full, pitch)
+            sums = full[:, :cols].double().sum(dim=1)
+            err = float((sums - 1.0).abs().max())
+            gather["max_rowsum_err"] = round(err, 6)
+            if err > 2e-3:
+                raise SystemExit(f"gathered matrix fails the row-sum check: {err}")
+        del recv
+
     # End to end through the host-buffer API.
     e2e = None
     if not args.no_e2e:
@@ -494,6 +547,7 @@ def main() -> int:
             "matrices_per_s": round(job_matrices / (ms_step / 1e3), 2),
             "roofline_pct": round(100.0 * value / (peak * world), 2),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "graph": graph,
+            "gather": gather,
             "gpu_launches": args.steps * world, "gpu_launches_per_rank": args.steps,
         }
         print(json.dumps(line), flush=True)
