@@ -20,7 +20,9 @@ value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
          consecutive launches touch more than 2 x L2 of memory.
 e2e    = the same metric through the host-buffer API (cs_session_softmax_host):
          pinned host input -> device -> kernel -> pinned host output per step,
-         host wall clock around the blocking call, max over ranks.
+         host wall clock around the blocking call, max over ranks. The call
+         moves only causal row blocks over PCIe (h2d/d2h bytes below) and
+         writes the output's masked tails with host threads.
 gather = N > 1 only: every rank's output shard sent to rank 0 over NCCL
          (NVLink), after the timed region; GB/s of the bytes rank 0 receives.
          For row blocks rank 0 assembles the matrix and checks its row sums.
@@ -521,9 +523,14 @@ def main() -> int:
         if world > 1:
             dist.all_reduce(e_step, op=dist.ReduceOp.MAX)
         e_s = float(e_step.item())
-        dense_bytes = job_matrices * rows_full * cols * 2  # all ranks
+        # Bytes the host path moved (causal row blocks), summed over ranks.
+        moved = torch.tensor([float(cs.host_copy_bytes(n_local, rows, cols, r0))], dtype=torch.float64,
+                             device="cuda")
+        if world > 1:
+            dist.all_reduce(moved)
+        moved_b = int(moved.item())
         e2e = {"value": round(alg_total / e_s / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": dense_bytes, "d2h_bytes_per_step": dense_bytes,
+               "h2d_bytes_per_step": moved_b, "d2h_bytes_per_step": moved_b,
                "ms_per_step": round(e_s * 1e3, 3),
                "timing": "host wall clock around the blocking call, max over ranks"}
 

@@ -148,6 +148,7 @@ def _declare(L) -> None:
         "cs_session_launch": (c_int, [vp, c_int, c_f32]),
         "cs_session_result": (c_int, [vp, u16p]),
         "cs_session_stream": (vp, [vp]),
+        "cs_host_copy_bytes": (c_i64, [c_i64, c_i32, c_i32, c_i32]),
         "cs_session_destroy": (None, [vp]),
         "cs_host_register": (c_int, [vp, sz]),
         "cs_host_unregister": (c_int, [vp]),
@@ -192,6 +193,11 @@ def kernel_id(kernel) -> int:
             raise CausalSoftmaxError(k, f"kernel {kernel!r}")
         return k
     return int(kernel)
+
+
+def host_copy_bytes(batch: int, rows: int, cols: int, row_offset: int = 0) -> int:
+    """Bytes Session.softmax_host moves in each direction (causal row blocks)."""
+    return int(lib().cs_host_copy_bytes(batch, rows, cols, row_offset))
 
 
 def padded_pitch(cols: int) -> int:

@@ -13,6 +13,8 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <thread>
+#include <vector>
 
 #include "causal_softmax.h"
 #include "kernels/baseline.cuh"
@@ -667,6 +669,61 @@ struct cs_session {
   bool prepared = false;
 };
 
+namespace {
+
+// The host path moves only causal bytes across PCIe: rows are sent in blocks
+// of kHostRowBlock, each with the width of its widest (last) row, in both
+// directions; rows that reach the full width go in one block. The masked
+// tail of each output row past its block's width is written +0.0 by host
+// threads while the copies run (disjoint bytes), instead of being copied.
+constexpr int32_t kHostRowBlock = 256;
+constexpr unsigned kMaxZeroThreads = 16;
+
+template <class F>
+void for_each_row_block(int32_t rows, int32_t cols, int32_t row_offset, F f) {
+  int64_t tri = (int64_t)cols - 1 - row_offset;  // rows with valid < cols
+  tri = tri < 0 ? 0 : (tri > rows ? rows : tri);
+  for (int32_t r0 = 0; r0 < tri; r0 += kHostRowBlock) {
+    const int32_t r1 = (int32_t)std::min<int64_t>(r0 + kHostRowBlock, tri);
+    f(r0, r1, (int32_t)std::min<int64_t>((int64_t)row_offset + r1, cols));
+  }
+  if (tri < rows) f((int32_t)tri, rows, cols);
+}
+
+// Bytes one direction of the host path carries for `batch` matrices.
+int64_t host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t row_offset) {
+  int64_t per = 0;
+  for_each_row_block(rows, cols, row_offset,
+                     [&](int32_t r0, int32_t r1, int32_t w) { per += (int64_t)(r1 - r0) * w * 2; });
+  return per * batch;
+}
+
+// Zero the masked tails [w, cols) of every output row on `nt` host threads.
+void zero_output_tails(uint16_t* h_out, int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
+                       std::vector<std::thread>& pool) {
+  std::vector<int32_t> width(rows);
+  bool any = false;
+  for_each_row_block(rows, cols, row_offset, [&](int32_t r0, int32_t r1, int32_t w) {
+    for (int32_t r = r0; r < r1; ++r) width[r] = w;
+    any |= w < cols;
+  });
+  if (!any) return;
+  const int64_t total_rows = batch * rows;
+  unsigned nt = std::max(1u, std::min(kMaxZeroThreads, std::thread::hardware_concurrency()));
+  nt = (unsigned)std::min<int64_t>(nt, total_rows);
+  for (unsigned t = 0; t < nt; ++t) {
+    pool.emplace_back([=, w = width]() {
+      for (int64_t i = total_rows * t / nt; i < total_rows * (t + 1) / nt; ++i) {
+        const int32_t r = (int32_t)(i % rows);
+        if (w[r] < cols)
+          std::memset(h_out + i * cols + w[r], 0, (size_t)(cols - w[r]) * 2);
+      }
+    });
+  }
+}
+
+}  // namespace
+
 extern "C" {
 
 int cs_abi_version(void) { return CS_ABI_VERSION; }
@@ -1070,6 +1127,11 @@ static int session_read_status(cs_session* s) {
   return (st & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
 }
 
+int64_t cs_host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t row_offset) {
+  if (batch <= 0 || rows <= 0 || cols <= 0 || row_offset < 0) return CS_ERR_EMPTY;
+  return host_copy_bytes(batch, rows, cols, row_offset);
+}
+
 int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
                             int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
                             float scale) {
@@ -1098,17 +1160,49 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     session->slot_bytes = need;
   }
   const size_t dpitch = (size_t)pitch * 2, hpitch = (size_t)cols * 2;
+  // Causal row blocks of one matrix, the same in both directions.
+  struct Block {
+    int32_t r0, r1, w;
+  };
+  std::vector<Block> blocks;
+  for_each_row_block(rows, cols, row_offset,
+                     [&](int32_t r0, int32_t r1, int32_t w) { blocks.push_back({r0, r1, w}); });
+  // Host threads zero the output's masked tails while the copies run.
+  std::vector<std::thread> zeroers;
+  zero_output_tails(h_out, batch, rows, cols, row_offset, zeroers);
+  auto join = [&]() {
+    for (auto& t : zeroers) t.join();
+    zeroers.clear();
+  };
+  auto copy_blocks = [&](uint8_t* dev, const uint8_t* host_src, uint8_t* host_dst, int64_t n,
+                         cudaMemcpyKind kind, cudaStream_t st) -> cudaError_t {
+    for (int64_t b = 0; b < n; ++b)
+      for (const Block& k : blocks) {
+        const size_t doff = ((size_t)b * rows + k.r0) * dpitch, hoff = ((size_t)b * rows + k.r0) * hpitch;
+        const cudaError_t e =
+            kind == cudaMemcpyHostToDevice
+                ? cudaMemcpy2DAsync(dev + doff, dpitch, host_src + hoff, hpitch, (size_t)k.w * 2,
+                                    (size_t)(k.r1 - k.r0), kind, st)
+                : cudaMemcpy2DAsync(host_dst + hoff, hpitch, dev + doff, dpitch, (size_t)k.w * 2,
+                                    (size_t)(k.r1 - k.r0), kind, st);
+        if (e != cudaSuccess) return e;
+      }
+    return cudaSuccess;
+  };
   for (int64_t c0 = 0, it = 0; c0 < batch; c0 += chunk, ++it) {
     const int slot = (int)(it & 1);
     cudaStream_t st = session->streams[slot];
     const int64_t n = std::min<int64_t>(chunk, batch - c0);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(h_in) + (size_t)c0 * mat_host;
     uint8_t* dst = reinterpret_cast<uint8_t*>(h_out) + (size_t)c0 * mat_host;
-    if (pitch == cols)
-      CS_CUDA(cudaMemcpyAsync(session->d_in[slot], src, (size_t)n * mat_host, cudaMemcpyHostToDevice, st));
-    else
-      CS_CUDA(cudaMemcpy2DAsync(session->d_in[slot], dpitch, src, hpitch, hpitch, (size_t)n * rows,
-                                cudaMemcpyHostToDevice, st));
+    cudaError_t ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_in[slot]), src, nullptr, n,
+                                 cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) {
+      cudaStreamSynchronize(session->streams[0]);
+      cudaStreamSynchronize(session->streams[1]);
+      join();
+      return cuda_fail(ce, "host-to-device copy");
+    }
     Geometry g{};
     g.in = session->d_in[slot];
     g.out = session->d_out[slot];
@@ -1122,19 +1216,23 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     g.status = session->d_status;
     g.timeout_ns = kDefaultTimeoutNs;
     rc = launch_geometry(session->device, kernel, g, Tuning{}, st, nullptr);
+    if (!rc) {
+      ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_out[slot]), nullptr, dst, n,
+                       cudaMemcpyDeviceToHost, st);
+      if (ce != cudaSuccess) rc = cuda_fail(ce, "device-to-host copy");
+    }
     if (rc) {
       cudaStreamSynchronize(session->streams[0]);
       cudaStreamSynchronize(session->streams[1]);
+      join();
       return rc;
     }
-    if (pitch == cols)
-      CS_CUDA(cudaMemcpyAsync(dst, session->d_out[slot], (size_t)n * mat_host, cudaMemcpyDeviceToHost, st));
-    else
-      CS_CUDA(cudaMemcpy2DAsync(dst, hpitch, session->d_out[slot], dpitch, hpitch, (size_t)n * rows,
-                                cudaMemcpyDeviceToHost, st));
   }
-  CS_CUDA(cudaStreamSynchronize(session->streams[0]));
-  CS_CUDA(cudaStreamSynchronize(session->streams[1]));
+  const cudaError_t e0 = cudaStreamSynchronize(session->streams[0]);
+  const cudaError_t e1 = cudaStreamSynchronize(session->streams[1]);
+  join();
+  if (e0 != cudaSuccess) return cuda_fail(e0, "cudaStreamSynchronize");
+  if (e1 != cudaSuccess) return cuda_fail(e1, "cudaStreamSynchronize");
   return session_read_status(session);
 }
 

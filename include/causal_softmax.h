@@ -258,11 +258,16 @@ int cs_session_probe(cs_session *session);
 /* End to end from host memory: `batch` dense rows x cols matrices (no
  * padding, like reference/src/lib.rs:85) are copied to the device with the
  * padded pitch, softmaxed, and copied back unpadded into h_out. Local row i
- * is absolute causal row row_offset + i (0 for whole matrices). Chunks of
- * matrices alternate between two streams so host->device copies, kernels and
- * device->host copies overlap; device buffers are cached in the session.
- * Pinned host memory (cs_host_register) makes the copies asynchronous.
- * Returns after the last copy has landed; checks the status word. */
+ * is absolute causal row row_offset + i (0 for whole matrices). Only causal
+ * bytes cross PCIe: rows travel in blocks of 256, each as wide as its widest
+ * row (cs_host_copy_bytes gives the bytes per direction), and the rest of
+ * each output row is written +0.0 by up to 16 host threads while the copies
+ * run; the input's masked part is never read. Chunks of matrices alternate
+ * between two streams so host->device copies, kernels and device->host
+ * copies overlap; device buffers are cached in the session. Pinned host
+ * memory (cs_host_register) makes the copies asynchronous. Returns after the
+ * last copy has landed and the zeroing threads have finished; checks the
+ * status word. */
 int cs_session_softmax_host(cs_session *session, int kernel, const uint16_t *h_in,
                             uint16_t *h_out, int64_t batch, int32_t rows, int32_t cols,
                             int32_t row_offset, float scale);
@@ -279,6 +284,12 @@ int cs_session_result(cs_session *session, uint16_t *h_out);
 
 /* The session's primary stream (cudaStream_t as void*). */
 void *cs_session_stream(cs_session *session);
+
+/* Bytes cs_session_softmax_host moves in each direction for `batch`
+ * rows x cols matrices starting at causal row row_offset (a host-only query;
+ * the reference copies whole matrices, gpu/src/driver.rs:65-95, 213-232).
+ * CS_ERR_EMPTY for non-positive sizes. */
+int64_t cs_host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t row_offset);
 
 void cs_session_destroy(cs_session *session);
 

@@ -275,3 +275,25 @@ def test_oracle_free_self_check():
     y2[3 * pitch + 10] = O.h(0.25)
     rep = cs.check_output(y2, batch=1, rows=rows, cols=cols, pitch=pitch)
     assert rep["mask_violations"] == 1
+
+
+def test_host_copy_bytes_cover_the_causal_prefixes():
+    # cs_session_softmax_host moves rows in blocks of 256, each as wide as its
+    # widest row; full-width rows in one block. Model it and check coverage.
+    def model(batch, rows, cols, off):
+        tri = min(max(cols - 1 - off, 0), rows)
+        per = 0
+        for r0 in range(0, tri, 256):
+            r1 = min(r0 + 256, tri)
+            per += (r1 - r0) * min(off + r1, cols) * 2
+        per += (rows - tri) * cols * 2
+        return per * batch
+    for batch, rows, cols, off in [(256, 4096, 4096, 0), (7, 300, 301, 0), (1, 100, 50, 2000),
+                                   (3, 1000, 1037, 0), (1, 4096, 32, 0), (2, 513, 4096, 3000),
+                                   (1, 1, 1, 0)]:
+        got = cs.host_copy_bytes(batch, rows, cols, off)
+        assert got == model(batch, rows, cols, off), (batch, rows, cols, off)
+        causal = sum(min(off + r + 1, cols) for r in range(rows)) * 2 * batch
+        assert causal <= got <= batch * rows * cols * 2
+    assert cs.host_copy_bytes(256, 4096, 4096) < 0.54 * 256 * 4096 * 4096 * 2
+    assert cs.host_copy_bytes(0, 4, 4) == cs.ERR_CODE["EMPTY"]

@@ -375,14 +375,19 @@ def test_session_paths():
             want = O.causal_softmax(dense, rows, cols, 0.125)[1]
             name, acc = O.verify(out, want, rows, cols)
             assert name == "ok", (kernel, name, acc.index)
-        # End to end from host buffers: equals the device path bit for bit.
-        batch, rows, cols = 7, 300, 301
-        xin = cs.generate(4, 3, batch=batch, rows=rows, cols=cols, pitch=cols)
-        hout = np.zeros_like(xin)
-        s.softmax_host(xin.ravel(), hout.reshape(-1), batch=batch, rows=rows, cols=cols, scale=0.2)
-        for b in (0, 3, 6):
-            dev = run("auto", O.pad(xin[b].ravel(), rows, cols).reshape(rows, -1), cols=cols, scale=0.2)
-            assert np.array_equal(O.unpad(dev.ravel(), rows, cols), hout[b].ravel())
+        # End to end from host buffers: equals the device path bit for bit,
+        # including the masked tails the host threads zero (the output starts
+        # as the 0xfb00 sentinel), for whole matrices and row blocks.
+        for batch, rows, cols, off in [(7, 300, 301, 0), (3, 700, 1037, 0), (2, 500, 600, 350),
+                                       (1, 40, 20, 100), (4, 600, 32, 0)]:
+            xin = cs.generate(4, 3, batch=batch, rows=rows, cols=cols, pitch=cols, first_row=off)
+            hout = np.full_like(xin, SENTINEL)
+            s.softmax_host(xin.ravel(), hout.reshape(-1), batch=batch, rows=rows, cols=cols, scale=0.2,
+                           row_offset=off)
+            for b in range(batch):
+                dev = run("auto", O.pad(xin[b].ravel(), rows, cols).reshape(rows, -1), cols=cols,
+                          scale=0.2, row_offset=off)
+                assert np.array_equal(O.unpad(dev.ravel(), rows, cols), hout[b].ravel()), (rows, cols, off, b)
 
 
 @pytest.mark.parametrize("kernel,tuning", [("tma", None), ("pipeline", None), ("online", None),
