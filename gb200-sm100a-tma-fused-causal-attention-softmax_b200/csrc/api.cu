@@ -1174,19 +1174,25 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     for (auto& t : zeroers) t.join();
     zeroers.clear();
   };
+  // One 3-D copy per row block covers the block in all n matrices of a chunk
+  // (depth = matrices), so the host issues a few dozen copies per chunk.
   auto copy_blocks = [&](uint8_t* dev, const uint8_t* host_src, uint8_t* host_dst, int64_t n,
                          cudaMemcpyKind kind, cudaStream_t st) -> cudaError_t {
-    for (int64_t b = 0; b < n; ++b)
-      for (const Block& k : blocks) {
-        const size_t doff = ((size_t)b * rows + k.r0) * dpitch, hoff = ((size_t)b * rows + k.r0) * hpitch;
-        const cudaError_t e =
-            kind == cudaMemcpyHostToDevice
-                ? cudaMemcpy2DAsync(dev + doff, dpitch, host_src + hoff, hpitch, (size_t)k.w * 2,
-                                    (size_t)(k.r1 - k.r0), kind, st)
-                : cudaMemcpy2DAsync(host_dst + hoff, hpitch, dev + doff, dpitch, (size_t)k.w * 2,
-                                    (size_t)(k.r1 - k.r0), kind, st);
-        if (e != cudaSuccess) return e;
-      }
+    const cudaPitchedPtr dp = make_cudaPitchedPtr(dev, dpitch, dpitch, (size_t)rows);
+    const cudaPitchedPtr hp = make_cudaPitchedPtr(
+        const_cast<uint8_t*>(kind == cudaMemcpyHostToDevice ? host_src : host_dst), hpitch, hpitch,
+        (size_t)rows);
+    for (const Block& k : blocks) {
+      cudaMemcpy3DParms m{};
+      m.srcPtr = kind == cudaMemcpyHostToDevice ? hp : dp;
+      m.dstPtr = kind == cudaMemcpyHostToDevice ? dp : hp;
+      m.srcPos = make_cudaPos(0, (size_t)k.r0, 0);
+      m.dstPos = make_cudaPos(0, (size_t)k.r0, 0);
+      m.extent = make_cudaExtent((size_t)k.w * 2, (size_t)(k.r1 - k.r0), (size_t)n);
+      m.kind = kind;
+      const cudaError_t e = cudaMemcpy3DAsync(&m, st);
+      if (e != cudaSuccess) return e;
+    }
     return cudaSuccess;
   };
   for (int64_t c0 = 0, it = 0; c0 < batch; c0 += chunk, ++it) {
