@@ -690,20 +690,50 @@ void for_each_row_block(int32_t rows, int32_t cols, int32_t row_offset, F f) {
   if (tri < rows) f((int32_t)tri, rows, cols);
 }
 
+// Chunks of the host path: whole matrices while one fits the chunk target
+// (1/8 of the job, between 8 and 256 MB of device buffer), else row blocks
+// of one matrix, each launched with its absolute row offset, so that copies
+// and kernels overlap on the two streams even for a single large matrix.
+constexpr int64_t kChunkMinBytes = int64_t(8) << 20, kChunkMaxBytes = int64_t(256) << 20;
+
+int32_t host_chunk_rows(int64_t batch, int32_t rows, int64_t pitch, int64_t* mats_per_chunk) {
+  const int64_t mat = (int64_t)rows * pitch * 2;
+  const int64_t job = batch > INT64_MAX / mat ? INT64_MAX : batch * mat;
+  const int64_t target = std::min(kChunkMaxBytes, std::max(kChunkMinBytes, job / 8));
+  if (mat <= target) {
+    *mats_per_chunk = std::max<int64_t>(1, std::min<int64_t>(batch, target / mat));
+    return rows;
+  }
+  *mats_per_chunk = 1;
+  return (int32_t)std::max<int64_t>(1, std::min<int64_t>(rows, target / (pitch * 2)));
+}
+
+// Causal row blocks of one matrix split into chunks of rc rows.
+template <class F>
+void for_each_copy_block(int32_t rows, int32_t cols, int32_t row_offset, int32_t rc, F f) {
+  for (int32_t r0 = 0; r0 < rows; r0 += rc) {
+    const int32_t n = std::min(rc, rows - r0);
+    for_each_row_block(n, cols, row_offset + r0,
+                       [&](int32_t a, int32_t b, int32_t w) { f(r0 + a, r0 + b, w); });
+  }
+}
+
 // Bytes one direction of the host path carries for `batch` matrices.
 int64_t host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t row_offset) {
+  int64_t mpc = 0;
+  const int32_t rc = host_chunk_rows(batch, rows, padded_pitch(cols), &mpc);
   int64_t per = 0;
-  for_each_row_block(rows, cols, row_offset,
-                     [&](int32_t r0, int32_t r1, int32_t w) { per += (int64_t)(r1 - r0) * w * 2; });
+  for_each_copy_block(rows, cols, row_offset, rc,
+                      [&](int32_t r0, int32_t r1, int32_t w) { per += (int64_t)(r1 - r0) * w * 2; });
   return per * batch;
 }
 
-// Zero the masked tails [w, cols) of every output row on `nt` host threads.
+// Zero the masked tails [w, cols) of every output row on host threads.
 void zero_output_tails(uint16_t* h_out, int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
-                       std::vector<std::thread>& pool) {
+                       int32_t rc, std::vector<std::thread>& pool) {
   std::vector<int32_t> width(rows);
   bool any = false;
-  for_each_row_block(rows, cols, row_offset, [&](int32_t r0, int32_t r1, int32_t w) {
+  for_each_copy_block(rows, cols, row_offset, rc, [&](int32_t r0, int32_t r1, int32_t w) {
     for (int32_t r = r0; r < r1; ++r) width[r] = w;
     any |= w < cols;
   });
@@ -1141,11 +1171,12 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
   if (rc) return rc;
   if (!is_known_kernel(kernel)) return CS_ERR_BAD_KERNEL;
   DeviceGuard guard(session->device);
-  const size_t mat_dev = (size_t)rows * (size_t)pitch * 2;
   const size_t mat_host = (size_t)rows * (size_t)cols * 2;
-  // Chunks of about 256 MB alternate between two streams/slots.
-  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(batch, (int64_t)((256u << 20) / mat_dev)));
-  const size_t need = (size_t)chunk * mat_dev;
+  const size_t dpitch = (size_t)pitch * 2, hpitch = (size_t)cols * 2;
+  // Chunks alternate between two streams/slots.
+  int64_t mpc = 0;
+  const int32_t crow = host_chunk_rows(batch, rows, pitch, &mpc);
+  const size_t need = (size_t)mpc * (size_t)crow * dpitch;
   if (need > session->slot_bytes) {
     for (int i = 0; i < 2; ++i) {
       if (session->d_in[i]) cudaFree(session->d_in[i]);
@@ -1159,29 +1190,25 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     }
     session->slot_bytes = need;
   }
-  const size_t dpitch = (size_t)pitch * 2, hpitch = (size_t)cols * 2;
-  // Causal row blocks of one matrix, the same in both directions.
-  struct Block {
-    int32_t r0, r1, w;
-  };
-  std::vector<Block> blocks;
-  for_each_row_block(rows, cols, row_offset,
-                     [&](int32_t r0, int32_t r1, int32_t w) { blocks.push_back({r0, r1, w}); });
   // Host threads zero the output's masked tails while the copies run.
   std::vector<std::thread> zeroers;
-  zero_output_tails(h_out, batch, rows, cols, row_offset, zeroers);
+  zero_output_tails(h_out, batch, rows, cols, row_offset, crow, zeroers);
   auto join = [&]() {
     for (auto& t : zeroers) t.join();
     zeroers.clear();
   };
-  // One 3-D copy per row block covers the block in all n matrices of a chunk
-  // (depth = matrices), so the host issues a few dozen copies per chunk.
-  auto copy_blocks = [&](uint8_t* dev, const uint8_t* host_src, uint8_t* host_dst, int64_t n,
+  struct Block {
+    int32_t r0, r1, w;
+  };
+  std::vector<Block> blocks;
+  // One 3-D copy per causal row block covers the block in all n matrices of
+  // a chunk (depth = matrices), so the host issues a few dozen copies per
+  // chunk. Host slices are whole matrices (rows x cols); device slices are
+  // the chunk's nr rows at the padded pitch.
+  auto copy_blocks = [&](uint8_t* dev, const uint8_t* host, int64_t n, int32_t nr,
                          cudaMemcpyKind kind, cudaStream_t st) -> cudaError_t {
-    const cudaPitchedPtr dp = make_cudaPitchedPtr(dev, dpitch, dpitch, (size_t)rows);
-    const cudaPitchedPtr hp = make_cudaPitchedPtr(
-        const_cast<uint8_t*>(kind == cudaMemcpyHostToDevice ? host_src : host_dst), hpitch, hpitch,
-        (size_t)rows);
+    const cudaPitchedPtr dp = make_cudaPitchedPtr(dev, dpitch, dpitch, (size_t)nr);
+    const cudaPitchedPtr hp = make_cudaPitchedPtr(const_cast<uint8_t*>(host), hpitch, hpitch, (size_t)rows);
     for (const Block& k : blocks) {
       cudaMemcpy3DParms m{};
       m.srcPtr = kind == cudaMemcpyHostToDevice ? hp : dp;
@@ -1195,43 +1222,45 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
     }
     return cudaSuccess;
   };
-  for (int64_t c0 = 0, it = 0; c0 < batch; c0 += chunk, ++it) {
-    const int slot = (int)(it & 1);
-    cudaStream_t st = session->streams[slot];
-    const int64_t n = std::min<int64_t>(chunk, batch - c0);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(h_in) + (size_t)c0 * mat_host;
-    uint8_t* dst = reinterpret_cast<uint8_t*>(h_out) + (size_t)c0 * mat_host;
-    cudaError_t ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_in[slot]), src, nullptr, n,
-                                 cudaMemcpyHostToDevice, st);
-    if (ce != cudaSuccess) {
-      cudaStreamSynchronize(session->streams[0]);
-      cudaStreamSynchronize(session->streams[1]);
-      join();
-      return cuda_fail(ce, "host-to-device copy");
-    }
-    Geometry g{};
-    g.in = session->d_in[slot];
-    g.out = session->d_out[slot];
-    g.batch = n;
-    g.batch_stride = (int64_t)rows * pitch;
-    g.rows = rows;
-    g.cols = cols;
-    g.pitch = (int32_t)pitch;
-    g.row_offset = row_offset;
-    g.scale = scale;
-    g.status = session->d_status;
-    g.timeout_ns = kDefaultTimeoutNs;
-    rc = launch_geometry(session->device, kernel, g, Tuning{}, st, nullptr);
-    if (!rc) {
-      ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_out[slot]), nullptr, dst, n,
-                       cudaMemcpyDeviceToHost, st);
-      if (ce != cudaSuccess) rc = cuda_fail(ce, "device-to-host copy");
-    }
-    if (rc) {
-      cudaStreamSynchronize(session->streams[0]);
-      cudaStreamSynchronize(session->streams[1]);
-      join();
-      return rc;
+  int64_t it = 0;
+  for (int64_t b0 = 0; b0 < batch; b0 += mpc) {
+    const int64_t n = std::min<int64_t>(mpc, batch - b0);
+    for (int32_t r0 = 0; r0 < rows; r0 += crow, ++it) {
+      const int32_t nr = std::min(crow, rows - r0);
+      const int slot = (int)(it & 1);
+      cudaStream_t st = session->streams[slot];
+      const size_t hoff = (size_t)b0 * mat_host + (size_t)r0 * hpitch;
+      blocks.clear();
+      for_each_row_block(nr, cols, row_offset + r0,
+                         [&](int32_t a, int32_t b, int32_t w) { blocks.push_back({a, b, w}); });
+      cudaError_t ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_in[slot]),
+                                   reinterpret_cast<const uint8_t*>(h_in) + hoff, n, nr,
+                                   cudaMemcpyHostToDevice, st);
+      if (ce == cudaSuccess) {
+        Geometry g{};
+        g.in = session->d_in[slot];
+        g.out = session->d_out[slot];
+        g.batch = n;
+        g.batch_stride = (int64_t)nr * pitch;
+        g.rows = nr;
+        g.cols = cols;
+        g.pitch = (int32_t)pitch;
+        g.row_offset = row_offset + r0;
+        g.scale = scale;
+        g.status = session->d_status;
+        g.timeout_ns = kDefaultTimeoutNs;
+        rc = launch_geometry(session->device, kernel, g, Tuning{}, st, nullptr);
+        if (!rc)
+          ce = copy_blocks(reinterpret_cast<uint8_t*>(session->d_out[slot]),
+                           reinterpret_cast<uint8_t*>(h_out) + hoff, n, nr, cudaMemcpyDeviceToHost, st);
+      }
+      if (ce != cudaSuccess) rc = cuda_fail(ce, "host path copy");
+      if (rc) {
+        cudaStreamSynchronize(session->streams[0]);
+        cudaStreamSynchronize(session->streams[1]);
+        join();
+        return rc;
+      }
     }
   }
   const cudaError_t e0 = cudaStreamSynchronize(session->streams[0]);

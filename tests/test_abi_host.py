@@ -280,20 +280,31 @@ def test_oracle_free_self_check():
 def test_host_copy_bytes_cover_the_causal_prefixes():
     # cs_session_softmax_host moves rows in blocks of 256, each as wide as its
     # widest row; full-width rows in one block. Model it and check coverage.
-    def model(batch, rows, cols, off):
+    # A matrix larger than the chunk target (1/8 of the job, 8..256 MB of
+    # device buffer) travels in row chunks, each blocked from its own offset.
+    def blocks(rows, cols, off):
         tri = min(max(cols - 1 - off, 0), rows)
         per = 0
         for r0 in range(0, tri, 256):
             r1 = min(r0 + 256, tri)
             per += (r1 - r0) * min(off + r1, cols) * 2
-        per += (rows - tri) * cols * 2
-        return per * batch
+        return per + (rows - tri) * cols * 2
+
+    def model(batch, rows, cols, off):
+        pitch = (cols + 7) // 8 * 8
+        mat = rows * pitch * 2
+        target = min(256 << 20, max(8 << 20, batch * mat // 8))
+        rc = rows if mat <= target else max(1, min(rows, target // (pitch * 2)))
+        return batch * sum(blocks(min(rc, rows - r0), cols, off + r0) for r0 in range(0, rows, rc))
+
     for batch, rows, cols, off in [(256, 4096, 4096, 0), (7, 300, 301, 0), (1, 100, 50, 2000),
                                    (3, 1000, 1037, 0), (1, 4096, 32, 0), (2, 513, 4096, 3000),
-                                   (1, 1, 1, 0)]:
+                                   (1, 1, 1, 0), (1, 8192, 8192, 0), (1, 32768, 32768, 0),
+                                   (1, 20000, 20001, 5), (1, 4096, 4096, 0)]:
         got = cs.host_copy_bytes(batch, rows, cols, off)
         assert got == model(batch, rows, cols, off), (batch, rows, cols, off)
-        causal = sum(min(off + r + 1, cols) for r in range(rows)) * 2 * batch
+        causal = (sum(min(off + r + 1, cols) for r in range(rows)) * 2 * batch if rows < 5000
+                  else 0)
         assert causal <= got <= batch * rows * cols * 2
     assert cs.host_copy_bytes(256, 4096, 4096) < 0.54 * 256 * 4096 * 4096 * 2
     assert cs.host_copy_bytes(0, 4, 4) == cs.ERR_CODE["EMPTY"]

@@ -379,7 +379,7 @@ def test_session_paths():
         # including the masked tails the host threads zero (the output starts
         # as the 0xfb00 sentinel), for whole matrices and row blocks.
         for batch, rows, cols, off in [(7, 300, 301, 0), (3, 700, 1037, 0), (2, 500, 600, 350),
-                                       (1, 40, 20, 100), (4, 600, 32, 0)]:
+                                       (1, 40, 20, 100), (4, 600, 32, 0), (1, 3000, 3001, 7)]:
             xin = cs.generate(4, 3, batch=batch, rows=rows, cols=cols, pitch=cols, first_row=off)
             hout = np.full_like(xin, SENTINEL)
             s.softmax_host(xin.ravel(), hout.reshape(-1), batch=batch, rows=rows, cols=cols, scale=0.2,
