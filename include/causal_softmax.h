@@ -261,7 +261,7 @@ int cs_session_probe(cs_session *session);
  * is absolute causal row row_offset + i (0 for whole matrices). Only causal
  * bytes cross PCIe: rows travel in blocks of 256, each as wide as its widest
  * row (cs_host_copy_bytes gives the bytes per direction), and the rest of
- * each output row is written +0.0 by up to 16 host threads while the copies
+ * each output row is written +0.0 by up to 8 host threads while the copies
  * run; the input's masked part is never read. Chunks of matrices alternate
  * between two streams so host->device copies, kernels and device->host
  * copies overlap; device buffers are cached in the session. Pinned host
