@@ -1,31 +1,37 @@
-// Row-resident single-pass causal softmax (the `tma` kernel choice).
+// Row-resident single-pass causal softmax (the `tma` and `pipeline` kernel
+// choices).
 //
 // Replaces the reference's three-pass TMA kernels (gpu/src/main.rs:202-541)
 // with one read of the causal prefix and one write of the full row:
 //
-//  * persistent grid (SM count x resident CTAs); CTA c takes work units
-//    c, c+G, c+2G, ... of the pair map in geometry.cuh, so every unit carries
-//    the same number of causal elements and the schedule is balanced statically;
+//  * persistent grid (SM count x resident CTAs) over the pair map in
+//    geometry.cuh, so every unit carries the same number of causal elements;
+//    CTA c starts with units c, c+G, ...; the register-resident variants keep
+//    that static sequence, the shared-memory variant (V == 0) claims the
+//    units after its first S from a per-plan counter (see the kernel);
 //  * warp-specialised: one producer warp streams each unit's row prefixes
 //    into a ring of shared-memory stages with 1-D TMA bulk copies
 //    (cp.async.bulk, completing on a `full` mbarrier per stage) and writes the
 //    masked columns and pitch padding with TMA bulk stores from a zeroed
 //    shared buffer; only round_up(valid, 8) elements are ever read;
-//  * consumer warps each own a contiguous segment of ONE row (32*V 16-byte
-//    vectors, lane-interleaved so every load/store instruction of a warp
-//    covers 512 contiguous bytes); a warp releases its stage (`empty`
-//    mbarrier) as soon as its vectors are in registers;
-//  * each warp reduces its own (max, sum) with shuffle butterflies -- the max
-//    on packed halves (exact), the exponents as (x - max) * scale*log2(e)
-//    with the Blackwell packed f32x2 add/mul, exp computed once per element
-//    with MUFU ex2 and kept in registers -- and publishes it; after ONE
-//    named barrier per unit the warps of a row merge the partials (online
-//    softmax rescaling) and write p = e * 2^((m_w - M)*scale*log2 e) / S;
-//  * partials are double-buffered, so that one barrier suffices.
+//  * register-resident consumers (V = 2, 4, 8) each own a contiguous segment
+//    of ONE row (32*V 16-byte vectors, lane-interleaved so every load/store
+//    instruction of a warp covers 512 contiguous bytes); a warp reduces its
+//    own (max, sum) with redux.sync -- the max on packed halves (exact), the
+//    exponents as (x - max) * scale*log2(e) with the Blackwell packed f32x2
+//    add/mul, exp computed once per element with MUFU ex2 and kept in
+//    registers -- and publishes it; after ONE named barrier per unit the
+//    warps of a row merge the partials (online-softmax rescaling) and write
+//    p = e * 2^((m_w - M)*scale*log2 e) / S; partials are double-buffered, so
+//    one barrier suffices;
+//  * shared-memory consumers (V = 0) leave the rows in the stage and make
+//    three passes (max, sum, normalise) over their chunk, for rows too long
+//    for registers (rowres_pass_consumers).
 //
-// The `pipeline` kernel choice is the same kernel with kTmaStore: consumers
-// write the normalised FP16 row back into the stage, and the producer warp
-// sends it with TMA bulk stores (shared->global) before refilling the stage.
+// With kTmaStore (`pipeline`) consumers write the normalised FP16 row back
+// into the stage, and the producer warp sends it with TMA bulk stores
+// (shared->global) before refilling the stage; without it (`tma`) consumers
+// store from registers.
 //
 // Every mbarrier wait is bounded (Geometry::timeout_ns); on expiry the kernel
 // sets kStatusTimeout in the status word, waits (bounded) for its own copies
