@@ -36,6 +36,7 @@ constexpr int kDefaultStages = 3;
 constexpr int64_t kRingBytesPerSm = 72 * 1024;  // row-resident ring bytes per SM (target)
 constexpr int kMaxAutoStages = 8;
 constexpr int kOnlineDefaultStages = 8;
+constexpr int kOnlineLongRowStages = 4;
 constexpr int64_t kI32Max = 2147483647;
 constexpr int64_t kMaxUnitsPerLaunch = int64_t(1) << 30;  // row-resident kernel, 32-bit unit index
 
@@ -381,6 +382,15 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
 
 int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
   int stages = t.stages ? t.stages : kOnlineDefaultStages;
+  if (!t.stages) {
+    // Rows too long to stay resident in half the default ring are fetched
+    // twice anyway; then a 4-stage ring, which lets 4 CTAs share an SM
+    // instead of 3, is faster (measured on B200 at 65536 and 98304 columns:
+    // 2.69 against 2.39 TB/s).
+    const int64_t widest = std::min<int64_t>((int64_t)g.row_offset + g.rows, g.cols);
+    const int64_t tiles = ((widest + 7) / 8 + cs::kOnlineTileVec - 1) / cs::kOnlineTileVec;
+    if (2 * tiles > kOnlineDefaultStages) stages = kOnlineLongRowStages;
+  }
   stages = std::max(1, std::min(stages, 24));
   while (stages > 1 && (int64_t)stages * cs::kOnlineTileBytes + cs::online_tail_bytes(stages) > d.max_smem_optin)
     --stages;
