@@ -777,17 +777,24 @@ void zero_output_tails(uint16_t* h_out, int64_t batch, int32_t rows, int32_t col
   const unsigned hw = std::thread::hardware_concurrency();
   unsigned nt = std::max(1u, std::min(kMaxZeroThreads, hw > 2 ? hw - 2 : 1u));
   nt = (unsigned)std::min<int64_t>(nt, total_rows);
-  for (unsigned t = 0; t < nt; ++t) {
-    pool.emplace_back([=, w = width]() {
-      for (int64_t i = total_rows * t / nt; i < total_rows * (t + 1) / nt; ++i) {
-        const int32_t r = (int32_t)(i % rows);
-        if (w[r] < cols)
-          zero_bytes(reinterpret_cast<uint8_t*>(h_out + i * cols + w[r]), (size_t)(cols - w[r]) * 2);
-      }
+  auto zero_share = [=](unsigned t, const std::vector<int32_t>& w) {
+    for (int64_t i = total_rows * t / nt; i < total_rows * (t + 1) / nt; ++i) {
+      const int32_t r = (int32_t)(i % rows);
+      if (w[r] < cols)
+        zero_bytes(reinterpret_cast<uint8_t*>(h_out + i * cols + w[r]), (size_t)(cols - w[r]) * 2);
+    }
 #if defined(__x86_64__)
-      _mm_sfence();  // streaming stores visible before the thread is joined
+    _mm_sfence();  // streaming stores visible before the thread is joined
 #endif
-    });
+  };
+  for (unsigned t = 0; t < nt; ++t) {
+    try {
+      pool.emplace_back([=]() { zero_share(t, width); });
+    } catch (...) {
+      // No thread to be had (resource limits): this share runs here instead,
+      // before the copies are issued; no exception leaves the C ABI.
+      zero_share(t, width);
+    }
   }
 }
 
@@ -1201,9 +1208,9 @@ int64_t cs_host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ro
   return host_copy_bytes(batch, rows, cols, row_offset);
 }
 
-int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
-                            int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
-                            float scale) {
+static int session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
+                                int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
+                                float scale) {
   if (!session || !h_in || !h_out) return CS_ERR_NULL;
   const int64_t pitch = padded_pitch(cols);
   int rc = validate_args(batch, (int64_t)rows * pitch, rows, cols, pitch, row_offset, scale);
@@ -1231,6 +1238,13 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
   }
   // Host threads zero the output's masked tails while the copies run.
   std::vector<std::thread> zeroers;
+  struct JoinAll {  // joins on every exit, including an exception
+    std::vector<std::thread>& v;
+    ~JoinAll() {
+      for (auto& t : v)
+        if (t.joinable()) t.join();
+    }
+  } join_all{zeroers};
   zero_output_tails(h_out, batch, rows, cols, row_offset, crow, zeroers);
   auto join = [&]() {
     for (auto& t : zeroers) t.join();
@@ -1308,6 +1322,21 @@ int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_i
   if (e0 != cudaSuccess) return cuda_fail(e0, "cudaStreamSynchronize");
   if (e1 != cudaSuccess) return cuda_fail(e1, "cudaStreamSynchronize");
   return session_read_status(session);
+}
+
+int cs_session_softmax_host(cs_session* session, int kernel, const uint16_t* h_in, uint16_t* h_out,
+                            int64_t batch, int32_t rows, int32_t cols, int32_t row_offset,
+                            float scale) {
+  try {
+    return session_softmax_host(session, kernel, h_in, h_out, batch, rows, cols, row_offset, scale);
+  } catch (...) {
+    if (session) {  // no copy may still be writing into the caller's buffers
+      cudaStreamSynchronize(session->streams[0]);
+      cudaStreamSynchronize(session->streams[1]);
+    }
+    std::snprintf(t_detail, sizeof t_detail, "host path: out of host memory or threads");
+    return CS_ERR_ARG;
+  }
 }
 
 int cs_session_prepare(cs_session* session, const uint16_t* h_in, int32_t rows, int32_t cols) {
