@@ -67,11 +67,16 @@ void parallel_rows(int64_t n, int threads, F&& fn) {
     return;
   }
   std::vector<std::thread> pool;
+  pool.reserve((size_t)threads);
   const int64_t per = (n + threads - 1) / threads;
   for (int t = 0; t < threads; ++t) {
     const int64_t a = t * per, e = std::min(n, a + per);
     if (a >= e) break;
-    pool.emplace_back([&fn, a, e] { fn(a, e); });
+    try {
+      pool.emplace_back([&fn, a, e] { fn(a, e); });
+    } catch (...) {
+      fn(a, e);  // no thread to be had: this range runs on the caller's thread
+    }
   }
   for (auto& th : pool) th.join();
 }
