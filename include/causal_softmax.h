@@ -104,7 +104,10 @@ int cs_kernel_supports(int kernel, int64_t cols);
 
 /* host/src/lib.rs:169-177 (Config::resolved_kernel) for this library:
  * WARP for cols <= 32, PIPELINE while a row pair (else a row) fits the row-resident kernel,
- * ONLINE beyond. Non-AUTO values are returned unchanged. */
+ * ONLINE beyond. Non-AUTO values are returned unchanged. Decides for whole
+ * matrices (row offset 0), like the reference; a plan for a row block decides
+ * with its own offset, so a block of long rows may resolve to ONLINE where
+ * this returns PIPELINE. */
 int cs_resolve_kernel(int kernel, int64_t rows, int64_t cols);
 
 /* host/src/lib.rs:49-64 (Kernel::logical_bytes) for this library's kernels:
