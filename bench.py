@@ -82,7 +82,9 @@ WORKLOADS = {
 
 
 def log(*a):
-    print(*a, file=sys.stderr, flush=True)
+    # One write per line, so that lines of concurrent ranks do not interleave.
+    sys.stderr.write(" ".join(str(x) for x in a) + "\n")
+    sys.stderr.flush()
 
 
 def f32(x: float) -> float:
@@ -386,6 +388,8 @@ def main() -> int:
         torch.cuda.synchronize()
     barrier()
     ms_total = start.elapsed_time(end)
+    log(f"rank {rank}: {ms_total / args.steps * 1e3:.1f} us per step, "
+        f"{info['algorithmic_bytes'] / (ms_total / args.steps * 1e6):.0f} GB/s on this rank's share")
     for p in plans:
         rc, st = p.status()
         if rc != 0:
