@@ -9,8 +9,12 @@ out), values half(N(0,1)*3) from seed 3, scale 1/sqrt(128). With N ranks (one
 process per GPU, launched by torchrun for N > 1) every rank runs its own batch
 of 256 independent heads (weak scaling: the job is N x 256 matrices). The
 single-matrix workloads (c1 4096^2, c2a 1000x1037 pitch 1040, c2b 4096x32, c3
-8192^2 stress, c5 32768^2) shard one matrix in row blocks balanced by causal
-area (row_offset per rank; strong scaling). There is no collective on the data
+8192^2 stress, c5 32768^2) shard one matrix over the ranks (strong scaling):
+rank k holds row block [t_k, t_k+1) and its mirror [M - t_k+1, M - t_k) of
+the M rows, stored one after the other (a folded plan: row_offset plus
+cs_plan_set_row_split), so each rank's row pairs are those of the whole
+matrix; --contiguous-rows (and matrices with more rows than columns) use
+contiguous blocks of equal causal cost. There is no collective on the data
 path: ranks meet only at the timing barriers.
 
 value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
@@ -76,8 +80,8 @@ WORKLOADS = {
                desc="stress 8192x8192 causal softmax, row blocks sharded over ranks"),
     "c5": dict(config=5, seed=4, matrices=1, rows=32768, cols=32768, pitch=32768,
                scale=INV_SQRT128, shard="rows", values="half(N(0,1)*2 + 0.001*c)",
-               desc="long context 32768x32768 causal softmax, row blocks balanced by causal "
-                    "area over ranks"),
+               desc="long context 32768x32768 causal softmax, folded row-block shards over "
+                    "ranks"),
 }
 
 
@@ -128,6 +132,25 @@ def row_blocks(rows: int, cols: int, parts: int) -> list[tuple[int, int]]:
         bounds.append(rows)
     bounds.append(rows)
     return [(bounds[i], bounds[i + 1]) for i in range(parts)]
+
+
+def rank_segments(rows: int, cols: int, parts: int, rank: int, fold: bool = True) -> list[tuple[int, int]]:
+    """Row segments (first absolute row, row count) of one rank's shard of a
+    single matrix, in the order they are stored.
+
+    Folded (rows <= cols, so every row but possibly the last is shorter than
+    the row width): rank k < parts-1 holds rows [t_k, t_k+1) and their mirror
+    [rows - t_k+1, rows - t_k), t_k = k * (rows // 2) // parts, and the last
+    rank the middle block [t_parts-1, rows - t_parts-1). Each shard's row pairs
+    then carry rows + 1 causal elements, as in the whole matrix, and the
+    shards are equal. Otherwise: contiguous blocks of equal causal cost."""
+    if not fold or rows > cols:
+        a, b = row_blocks(rows, cols, parts)[rank]
+        return [(a, b - a)]
+    t = [k * (rows // 2) // parts for k in range(parts)]
+    if rank == parts - 1:
+        return [(t[rank], rows - 2 * t[rank])]
+    return [(t[rank], t[rank + 1] - t[rank]), (rows - t[rank + 1], t[rank + 1] - t[rank])]
 
 
 class ClockSampler:
@@ -281,6 +304,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true",
                     help="N > 1: skip the separately reported gather of all outputs to rank 0")
+    ap.add_argument("--contiguous-rows", action="store_true",
+                    help="single matrices: contiguous row blocks instead of folded shards")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the CUDA-graph timing of the single-matrix workloads")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -328,30 +353,39 @@ def main() -> int:
         # (matrices rank*M .. rank*M + M - 1 of the seeded stream); there is
         # no exchange between ranks on this path.
         n_local, first_b = w["matrices"], rank * w["matrices"]
-        r0, r1 = 0, rows_full
+        segs = [(0, rows_full)]
         scaling, job_matrices = "weak", w["matrices"] * world
     else:
-        # Strong scaling: the rows of one matrix, in blocks of equal causal cost.
+        # Strong scaling: the rows of one matrix, as a folded shard (a row
+        # block and its mirror, stored one after the other) or one block.
         n_local, first_b = w["matrices"], 0
-        r0, r1 = row_blocks(rows_full, cols, world)[rank]
+        segs = rank_segments(rows_full, cols, world, rank, fold=not args.contiguous_rows)
         scaling, job_matrices = "strong", w["matrices"]
-    rows = r1 - r0
+    rows = sum(n for _, n in segs)
+    r0 = segs[0][0]
 
     # This rank's input on the host (pinned) and on the device; rotate copies
     # when one copy (in + out) is smaller than 2 x L2.
     t0 = time.perf_counter()
     h_in = torch.empty((n_local, rows, pitch), dtype=torch.int16, pin_memory=True)
-    cs.generate(w["config"], w["seed"], batch=n_local, rows=rows, cols=cols, pitch=pitch,
-                first_batch=first_b, first_row=r0, out=h_in.numpy().view(np.uint16))
+    off = 0
+    for a, n in segs:  # one segment per matrix batch, or n_local == 1
+        cs.generate(w["config"], w["seed"], batch=n_local, rows=n, cols=cols, pitch=pitch,
+                    first_batch=first_b, first_row=a, out=h_in.numpy().view(np.uint16)[:, off:off + n])
+        off += n
     copy_bytes = 2 * h_in.numel() * 2
     n_rot = 1 if copy_bytes >= 2 * L2_BYTES else math.ceil(2 * L2_BYTES / copy_bytes) + 1
     d_in = [h_in.cuda().view(torch.float16) for _ in range(n_rot)]
     d_out = [torch.empty_like(d_in[0]) for _ in range(n_rot)]
-    log(f"rank {rank}: matrices {first_b}..{first_b + n_local} rows {r0}..{r1} x {cols}, "
+    seg_text = " + ".join(f"{a}..{a + n}" for a, n in segs)
+    log(f"rank {rank}: matrices {first_b}..{first_b + n_local} rows {seg_text} x {cols}, "
         f"{n_rot} buffer set(s), ready in {time.perf_counter() - t0:.1f} s")
 
     stream = torch.cuda.current_stream()
     plans = [cs.Plan.for_tensors(a, b, cols=cols, row_offset=r0) for a, b in zip(d_in, d_out)]
+    if len(segs) > 1:
+        for p in plans:
+            p.set_row_split(segs[0][1], segs[1][0])
     if args.tuning:
         for p in plans:
             p.set_tuning(*(int(t) for t in args.tuning.split(",")))
@@ -373,9 +407,13 @@ def main() -> int:
     # Spot check of the timed kernel's output (oracle-free structure check).
     nchk = min(2, n_local)
     host_out = d_out[0][:nchk].view(torch.int16).cpu().numpy().view(np.uint16)
-    chk = cs.check_output(host_out, batch=nchk, rows=rows, cols=cols, pitch=pitch, row_offset=r0)
-    if chk["mask_violations"] or chk["nonfinite_or_negative"] or chk["rowsum_violations"]:
-        raise SystemExit(f"output self-check failed: {chk}")
+    off = 0
+    for a, n in segs:
+        chk = cs.check_output(host_out[:, off:off + n], batch=nchk, rows=n, cols=cols, pitch=pitch,
+                              row_offset=a)
+        off += n
+        if chk["mask_violations"] or chk["nonfinite_or_negative"] or chk["rowsum_violations"]:
+            raise SystemExit(f"output self-check failed (rows {a}..{a + n}): {chk}")
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -492,7 +530,13 @@ def main() -> int:
                   "bytes": moved, "ms": round(float(gt.item()), 3),
                   "timing": "NCCL send/recv of every rank's output to rank 0, device time, max over ranks"}
         if rank == 0 and w["shard"] == "rows":
-            full = recv.reshape(rows_full, pitch)
+            # Place every rank's segments at their rows.
+            full = torch.empty((rows_full, pitch), dtype=torch.float16, device="cuda")
+            pos = 0
+            for r in range(world):
+                for a, n in rank_segments(rows_full, cols, world, r, fold=not args.contiguous_rows):
+                    full[a:a + n].copy_(recv[pos:pos + n * pitch].view(n, pitch))
+                    pos += n * pitch
             sums = full[:, :cols].double().sum(dim=1)
             err = float((sums - 1.0).abs().max())
             gather["max_rowsum_err"] = round(err, 6)
@@ -511,25 +555,37 @@ def main() -> int:
             dense_in = torch.empty((n_local, rows, cols), dtype=torch.int16, pin_memory=True)
             dense_in.copy_(h_in[:, :, :cols])
         dense_out = torch.empty_like(dense_in, pin_memory=True)
-        hin = dense_in.numpy().view(np.uint16).reshape(-1)
-        hout = dense_out.numpy().view(np.uint16).reshape(-1)
+        # One host-path call per segment of the shard (views into the
+        # pinned buffers; a folded shard has two).
+        calls, off = [], 0
+        for a, n in segs:
+            si = dense_in.numpy().view(np.uint16)[:, off:off + n]
+            so = dense_out.numpy().view(np.uint16)[:, off:off + n]
+            if not (si.flags.c_contiguous and so.flags.c_contiguous):
+                raise SystemExit("host-path segments must be contiguous (one matrix per folded shard)")
+            calls.append((si.reshape(-1), so.reshape(-1), n, a))
+            off += n
+
+        def host_step(sess):
+            for si, so, n, a in calls:
+                sess.softmax_host(si, so, batch=n_local, rows=n, cols=cols, scale=scale,
+                                  kernel=args.kernel, row_offset=a)
+
         with cs.Session(local) as sess:
-            sess.softmax_host(hin, hout, batch=n_local, rows=rows, cols=cols, scale=scale,
-                              kernel=args.kernel, row_offset=r0)  # warm-up: allocates buffers
+            host_step(sess)  # warm-up: allocates buffers
             times = []
             for _ in range(max(1, args.e2e_steps)):
                 barrier()
                 t0 = time.perf_counter()
-                sess.softmax_host(hin, hout, batch=n_local, rows=rows, cols=cols, scale=scale,
-                                  kernel=args.kernel, row_offset=r0)
+                host_step(sess)
                 times.append(time.perf_counter() - t0)
         e_step = torch.tensor([statistics.mean(times)], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(e_step, op=dist.ReduceOp.MAX)
         e_s = float(e_step.item())
         # Bytes the host path moved (causal row blocks), summed over ranks.
-        moved = torch.tensor([float(cs.host_copy_bytes(n_local, rows, cols, r0))], dtype=torch.float64,
-                             device="cuda")
+        moved = torch.tensor([float(sum(cs.host_copy_bytes(n_local, n, cols, a) for a, n in segs))],
+                             dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(moved)
         moved_b = int(moved.item())

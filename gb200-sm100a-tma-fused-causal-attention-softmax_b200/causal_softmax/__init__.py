@@ -131,6 +131,7 @@ def _declare(L) -> None:
         "cs_plan_launch": (c_int, [vp, c_int, c_f32, vp]),
         "cs_plan_status": (c_int, [vp, ctypes.POINTER(ctypes.c_uint32)]),
         "cs_plan_set_timeout": (c_int, [vp, ctypes.c_uint64]),
+        "cs_plan_set_row_split": (c_int, [vp, c_i32, c_i32]),
         "cs_plan_set_tuning": (c_int, [vp, c_int, c_int, c_int, c_int]),
         "cs_plan_describe": (c_int, [vp, c_int, ctypes.POINTER(LaunchInfo)]),
         "cs_plan_launch_debug": (c_int, [vp, c_int, c_f32, vp, ctypes.c_uint32, ctypes.c_uint64]),
@@ -267,6 +268,12 @@ class Plan:
 
     def set_timeout(self, ns: int) -> None:
         check(lib().cs_plan_set_timeout(self._h, ns), "cs_plan_set_timeout")
+
+    def set_row_split(self, split_row: int, split_offset: int) -> None:
+        """Local rows split_row.. are absolute rows split_offset.. (a folded
+        shard: a row block and its mirror); split_row 0 undoes it."""
+        check(lib().cs_plan_set_row_split(self._h, split_row, split_offset),
+              "cs_plan_set_row_split")
 
     def set_tuning(self, vec: int = 0, stages: int = 0, l2_hint: int = -1,
                    zero_fill_tma: int = -1) -> None:

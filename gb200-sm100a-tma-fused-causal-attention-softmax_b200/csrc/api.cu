@@ -173,6 +173,14 @@ double causal_elements(int64_t rows, int64_t cols, int64_t row_offset) {
   return t * (double)(row_offset + 1) + t * (t - 1.0) / 2.0 + (double)(rows - tri) * (double)cols;
 }
 
+// Causal element count of a launch's rows (both row blocks of a folded one),
+// with rows clipped to `cols` columns.
+double geometry_causal_elements(const Geometry& g, int64_t cols) {
+  const double first = g.split_row > 0 ? causal_elements(g.split_row, cols, g.row_offset) : 0.0;
+  return first + causal_elements((int64_t)g.rows - g.split_row, cols,
+                                 (int64_t)g.row_offset + g.split_row + g.split_shift);
+}
+
 int validate_args(int64_t batch, int64_t batch_stride, int64_t rows, int64_t cols, int64_t pitch,
                   int64_t row_offset, float scale) {
   if (batch <= 0 || rows <= 0 || cols <= 0) return CS_ERR_EMPTY;
@@ -211,13 +219,7 @@ struct LaunchPlan {
   cs::BaselineParams bl{};
 };
 
-int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) {
-  int64_t mx = 0;
-  if (m.n_pairs > 0) mx = std::max(mx, (2 * (int64_t)g.row_offset + m.n_tri + 1 + 7) / 8 + 1);
-  if (m.n_tri & 1) mx = std::max(mx, ((int64_t)g.row_offset + m.n_pairs + 1 + 7) / 8);
-  if (g.rows > m.n_tri) mx = std::max(mx, ((int64_t)g.cols + 7) / 8);
-  return mx;
-}
+int64_t rowres_max_vectors(const Geometry& g, const cs::UnitMap& m) { return cs::unit_max_vectors(g, m); }
 
 // CTA size of variant i for units of up to max_nv vectors: each consumer
 // warp owns 32*V vectors of one row, a row pair needs one warp more than its
@@ -387,7 +389,7 @@ int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchP
     // twice anyway; then a 4-stage ring, which lets 4 CTAs share an SM
     // instead of 3, is faster (measured on B200 at 65536 and 98304 columns:
     // 2.69 against 2.39 TB/s).
-    const int64_t widest = std::min<int64_t>((int64_t)g.row_offset + g.rows, g.cols);
+    const int64_t widest = std::min<int64_t>(cs::abs_row(g, g.rows - 1) + 1, g.cols);
     const int64_t tiles = ((widest + 7) / 8 + cs::kOnlineTileVec - 1) / cs::kOnlineTileVec;
     if (2 * tiles > kOnlineDefaultStages) stages = kOnlineLongRowStages;
   }
@@ -477,12 +479,12 @@ struct PlanKey {
   int kernel;
   Tuning t;
   int64_t batch, batch_stride;
-  int32_t rows, cols, pitch, row_offset;
+  int32_t rows, cols, pitch, row_offset, split_row, split_shift;
   bool operator==(const PlanKey& o) const {
     return dev == o.dev && kernel == o.kernel && t.vec == o.t.vec && t.stages == o.t.stages &&
            t.hint == o.t.hint && t.zero_tma == o.t.zero_tma && batch == o.batch &&
            batch_stride == o.batch_stride && rows == o.rows && cols == o.cols && pitch == o.pitch &&
-           row_offset == o.row_offset;
+           row_offset == o.row_offset && split_row == o.split_row && split_shift == o.split_shift;
   }
 };
 constexpr int kPlanCacheSize = 16;
@@ -491,7 +493,8 @@ thread_local LaunchPlan t_plans[kPlanCacheSize];
 thread_local int t_plan_count = 0, t_plan_next = 0;
 
 int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
-  const PlanKey key{&d, kernel, t, g.batch, g.batch_stride, g.rows, g.cols, g.pitch, g.row_offset};
+  const PlanKey key{&d, kernel, t, g.batch, g.batch_stride, g.rows, g.cols, g.pitch, g.row_offset,
+                    g.split_row, g.split_shift};
   for (int i = 0; i < t_plan_count; ++i) {
     if (t_plan_keys[i] == key) {
       *lp = t_plans[i];
@@ -578,7 +581,7 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
 }
 
 double modelled_bytes(int kernel, const Geometry& g, int online_stages) {
-  const double t = causal_elements(g.rows, g.cols, g.row_offset);
+  const double t = geometry_causal_elements(g, g.cols);
   const double w = 2.0 * (double)g.rows * (double)g.cols;
   double per = 0;
   switch (kernel) {
@@ -587,7 +590,7 @@ double modelled_bytes(int kernel, const Geometry& g, int online_stages) {
       // Rows longer than half the ring are fetched twice.
       const int64_t resident_cols = (int64_t)(online_stages / 2) * cs::kOnlineTileVec * 8;
       const double t_long = g.cols > resident_cols
-                                ? std::max(0.0, t - causal_elements(g.rows, std::min<int64_t>(g.cols, resident_cols), g.row_offset))
+                                ? std::max(0.0, t - geometry_causal_elements(g, std::min<int64_t>(g.cols, resident_cols)))
                                 : 0.0;
       per = 2.0 * t + 2.0 * t_long + w;
       break;
@@ -957,6 +960,30 @@ int cs_plan_set_timeout(cs_plan* plan, uint64_t timeout_ns) {
   return CS_OK;
 }
 
+int cs_plan_set_row_split(cs_plan* plan, int32_t split_row, int32_t split_offset) {
+  if (!plan) return CS_ERR_NULL;
+  if (split_row == 0) {
+    plan->g.split_row = 0;
+    plan->g.split_shift = 0;
+    return CS_OK;
+  }
+  const Geometry& g = plan->g;
+  // The second block starts at or after the first one's end (absolute rows
+  // increase with the local row) and stays within 32-bit row indices.
+  if (split_row < 0 || split_row >= g.rows || split_offset < 0 ||
+      (int64_t)split_offset < (int64_t)g.row_offset + split_row ||
+      (int64_t)split_offset > kI32Max - ((int64_t)g.rows - split_row)) {
+    std::snprintf(t_detail, sizeof t_detail,
+                  "row split %d at absolute row %d: needs 0 < split_row < rows (%d) and a second block "
+                  "starting at or after row %lld",
+                  (int)split_row, (int)split_offset, (int)g.rows, (long long)g.row_offset + split_row);
+    return CS_ERR_ARG;
+  }
+  plan->g.split_row = split_row;
+  plan->g.split_shift = (int32_t)((int64_t)split_offset - g.row_offset - split_row);
+  return CS_OK;
+}
+
 int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint, int zero_fill_tma) {
   if (!plan) return CS_ERR_NULL;
   const bool variant_pick = vec_per_thread >= 16 && vec_per_thread < 16 + kNumRowVariants;
@@ -1025,7 +1052,8 @@ int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
   info->launches = 1;
   info->units = lp.units;
   info->algorithmic_bytes =
-      cs_roofline_bytes(plan->g.rows, plan->g.cols, plan->g.row_offset) * (double)plan->g.batch;
+      (2.0 * geometry_causal_elements(plan->g, plan->g.cols) + 2.0 * (double)plan->g.rows * plan->g.cols) *
+      (double)plan->g.batch;
   info->modelled_bytes = modelled_bytes(lp.kernel, plan->g, lp.stages ? lp.stages : kOnlineDefaultStages);
   return CS_OK;
 }

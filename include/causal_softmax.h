@@ -170,6 +170,18 @@ int cs_plan_status(cs_plan *plan, uint32_t *status);
  * launches of this plan (default 2 s). */
 int cs_plan_set_timeout(cs_plan *plan, uint64_t timeout_ns);
 
+/* Folded row-block shard (no counterpart in the reference, which has no
+ * multi-GPU path; extends the row_offset of cs_plan_create): local rows
+ * split_row..rows-1 of every matrix are absolute causal rows split_offset,
+ * split_offset+1, ... — a second row block stored right after the first.
+ * For an M-row causal matrix over N ranks, rank k holding block [a, b) and
+ * its mirror [M-b, M-a) (split_row = b - a, split_offset = M - b) gets units
+ * of M+1 causal elements each, as the whole matrix does, instead of a block
+ * of only the longest rows. Needs 0 < split_row < rows and split_offset >=
+ * row_offset + split_row (else CS_ERR_ARG); split_row = 0 restores one
+ * contiguous block. Affects later launches of the plan. */
+int cs_plan_set_row_split(cs_plan *plan, int32_t split_row, int32_t split_offset);
+
 /* Tuning knobs (0 / -1 = automatic): vectors per thread of the TMA /
  * PIPELINE kernels (2, 4 or 8; 16 + i selects compiled variant i of the
  * row-resident kernel directly), ring stages of the TMA / PIPELINE / ONLINE

@@ -220,6 +220,104 @@ def test_row_block_shards_match_full_matrix(kernel):
             assert diff.max() == 0, (kernel, a, b)
 
 
+def run_folded(kernel: str, x: np.ndarray, segs, *, cols: int, scale: float, tuning=None) -> np.ndarray:
+    """One launch over a folded shard: x holds the segments' rows one after
+    the other; the plan maps them with row_offset and cs_plan_set_row_split."""
+    d_in = to_dev(x)
+    d_out = sentinel_like(d_in)
+    with cs.Plan.for_tensors(d_in, d_out, cols=cols, row_offset=segs[0][0]) as plan:
+        if len(segs) > 1:
+            plan.set_row_split(segs[0][1], segs[1][0])
+        if tuning:
+            plan.set_tuning(*tuning)
+        plan.launch(kernel, scale)
+        rc, status = plan.status()
+        assert rc == 0 and status == 0, (rc, status)
+    torch.cuda.synchronize()
+    return from_dev(d_out)
+
+
+FOLD_CASES = [(4096, 4096, 4), (1001, 1001, 3), (300, 20000, 2), (4096, 4096, 8)]
+
+
+@pytest.mark.parametrize("kernel", ["baseline", "tma", "pipeline", "online", "auto"])
+def test_folded_shards_match_full_matrix(kernel):
+    # A rank's folded shard (row block [a, b) and its mirror, stored one after
+    # the other) reproduces those rows of the full launch: each segment passes
+    # the oracle check on its absolute rows and agrees with the full matrix
+    # within one FP16 ulp (bit for bit for the kernels whose per-row work does
+    # not depend on how rows are grouped into units).
+    import bench
+
+    for rows, cols, parts in FOLD_CASES:
+        scale = float(np.float32(1 / np.sqrt(128)))
+        x = cs.generate(1, 0, batch=1, rows=rows, cols=cols)[0]
+        full = run(kernel, x, cols=cols, scale=scale)
+        for r in range(parts):
+            segs = bench.rank_segments(rows, cols, parts, r)
+            xl = np.concatenate([x[a:a + n] for a, n in segs])
+            got = run_folded(kernel, xl, segs, cols=cols, scale=scale)
+            o = 0
+            for a, n in segs:
+                what = f"{kernel} {rows}x{cols} rank {r}/{parts} rows {a}:{a + n}"
+                check(got[o:o + n], x[a:a + n], cols=cols, scale=scale, row_offset=a, what=what)
+                diff = np.abs(got[o:o + n].astype(np.int32) - full[a:a + n].astype(np.int32))
+                assert diff.max() <= (0 if kernel in ("baseline", "online") else 1), what
+                o += n
+
+
+@pytest.mark.parametrize("variant", range(8))
+def test_folded_shards_every_row_resident_variant(variant):
+    import bench
+
+    for rows, cols, parts in [(2000, 2000, 4), (300, 20000, 2)]:
+        x = cs.generate(2, 5, batch=1, rows=rows, cols=cols)[0]
+        for r in range(parts):
+            segs = bench.rank_segments(rows, cols, parts, r)
+            xl = np.concatenate([x[a:a + n] for a, n in segs])
+            try:
+                got = run_folded("pipeline", xl, segs, cols=cols, scale=0.0883883,
+                                 tuning=(16 + variant, 0, -1, -1))
+            except cs.CausalSoftmaxError as e:
+                assert e.code == cs.ERR_CODE["UNSUPPORTED"] and variant != 7, e
+                continue
+            o = 0
+            for a, n in segs:
+                check(got[o:o + n], x[a:a + n], cols=cols, scale=0.0883883, row_offset=a,
+                      what=f"variant {variant} {rows}x{cols} rank {r} rows {a}:{a + n}")
+                o += n
+
+
+def test_folded_narrow_rows_and_split_errors():
+    import bench
+
+    # The warp path (cols <= 32) under a fold.
+    x = cs.generate(2, 1, batch=1, rows=32, cols=32)[0]
+    for r in range(2):
+        segs = bench.rank_segments(32, 32, 2, r)
+        xl = np.concatenate([x[a:a + n] for a, n in segs])
+        for kernel in ("warp", "auto"):
+            got = run_folded(kernel, xl, segs, cols=32, scale=0.5)
+            o = 0
+            for a, n in segs:
+                check(got[o:o + n], x[a:a + n], cols=32, scale=0.5, row_offset=a, what=f"{kernel} rank {r}")
+                o += n
+    # Argument checks of cs_plan_set_row_split.
+    E = cs.ERR_CODE
+    d_in = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
+    d_out = torch.zeros_like(d_in)
+    L = cs.lib()
+    with cs.Plan.for_tensors(d_in, d_out, cols=64, row_offset=10) as plan:
+        h = plan._h
+        assert L.cs_plan_set_row_split(h, 64, 200) == E["ARG"]   # no rows left for the second block
+        assert L.cs_plan_set_row_split(h, -1, 200) == E["ARG"]
+        assert L.cs_plan_set_row_split(h, 16, 25) == E["ARG"]    # overlaps the first block (ends at 26)
+        assert L.cs_plan_set_row_split(h, 16, 2**31 - 40) == E["ARG"]  # past 32-bit rows
+        assert L.cs_plan_set_row_split(None, 16, 26) == E["NULL"]
+        assert L.cs_plan_set_row_split(h, 16, 26) == 0           # contiguous: same as no split
+        assert L.cs_plan_set_row_split(h, 0, 0) == 0             # back to one block
+
+
 def test_deterministic_and_kernels_agree():
     rows, cols = 777, 1500
     x = cs.generate(2, 1, batch=1, rows=rows, cols=cols)[0]

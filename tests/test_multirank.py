@@ -42,6 +42,18 @@ def _worker(rank: int, world: int, port: int, q):
         y = O.softmax_strided(x.ravel(), 1, 0, b - a, cols, pitch, a, 1.0).reshape(b - a, pitch)
         parts = [None] * world
         dist.all_gather_object(parts, (a, b, y))
+        # Folded shards (a row block and its mirror, stored one after the
+        # other), laid out as bench.py lays out a rank's buffer.
+        fr, fc = 301, 320  # folding needs rows <= cols; an odd count leaves a middle row
+        fp = cs.padded_pitch(fc)
+        segs = bench.rank_segments(fr, fc, world, rank)
+        xf = np.concatenate([cs.generate(3, 2, batch=1, rows=n, cols=fc, first_row=s0)[0]
+                             for s0, n in segs])
+        yf = np.concatenate([O.softmax_strided(xf[o:o + n].ravel(), 1, 0, n, fc, fp, s0, 1.0)
+                             .reshape(n, fp)
+                             for (s0, n), o in zip(segs, np.cumsum([0] + [n for _, n in segs]))])
+        fparts = [None] * world
+        dist.all_gather_object(fparts, yf)
         # Heads (the batched workload).
         heads, hr = 6, 40
         hp = cs.padded_pitch(hr)
@@ -54,7 +66,7 @@ def _worker(rank: int, world: int, port: int, q):
         t = torch.tensor([float(rank + 1)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         if rank == 0:
-            q.put((parts, hparts, float(t.item())))
+            q.put((parts, fparts, hparts, float(t.item())))
     finally:
         dist.destroy_process_group()
 
@@ -71,7 +83,7 @@ def test_sharded_results_equal_unsharded():
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    parts, hparts, tmax = q.get(timeout=300)
+    parts, fparts, hparts, tmax = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -83,6 +95,20 @@ def test_sharded_results_equal_unsharded():
     full = O.softmax_strided(x.ravel(), 1, 0, rows, cols, pitch, 0, 1.0).reshape(rows, pitch)
     assert [p[0] for p in parts] == [0, parts[0][1]] and parts[-1][1] == rows
     assert np.array_equal(np.concatenate([p[2] for p in parts]), full)
+    # Folded shards put back at their rows give the same matrix.
+    fr, fc = 301, 320
+    fp = cs.padded_pitch(fc)
+    xf = cs.generate(3, 2, batch=1, rows=fr, cols=fc)[0]
+    ffull = O.softmax_strided(xf.ravel(), 1, 0, fr, fc, fp, 0, 1.0).reshape(fr, fp)
+    assembled = np.full_like(ffull, 0xFFFF)
+    for r in range(world):
+        o = 0
+        for s0, n in bench.rank_segments(fr, fc, world, r):
+            assembled[s0:s0 + n] = fparts[r][o:o + n]
+            o += n
+        assert o == len(fparts[r])
+    assert len(bench.rank_segments(fr, fc, world, 0)) == 2  # rank 0's shard is folded
+    assert np.array_equal(assembled, ffull)
 
     heads, hr = 6, 40
     hp = cs.padded_pitch(hr)
