@@ -32,6 +32,8 @@ gather = N > 1 only: every rank's output shard sent to rank 0 over NCCL
          For row blocks rank 0 assembles the matrix and checks its row sums.
 graph  = single-matrix workloads only: the same launches captured k at a time
          in a CUDA graph, device time per launch (labelled; not the value).
+launch_stats = min / median / p95 / max of single launches (the reference's
+         BenchStats), from a separate pass with an event after each launch.
 roofline  = the single kernel's per-launch algorithmic bytes / per-launch time
             against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
 cpu_baseline = the reference CPU path (C restatement of
@@ -452,6 +454,29 @@ def main() -> int:
                           f"vec={info['vec_per_thread']}"}
     clk = clocks.summary()
 
+    # Per-launch distribution (the reference's BenchStats: min / median / p95)
+    # from a separate pass with an event after every launch; `value` comes
+    # from the uninterrupted timed region above.
+    launch_stats = None
+    try:
+        n_s = max(20, min(args.steps, 200))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_s + 1)]
+        ev[0].record(stream)
+        for i in range(n_s):
+            plans[i % n_rot].launch(args.kernel, scale, stream)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        st = cs.bench_stats([ev[i].elapsed_time(ev[i + 1]) for i in range(n_s)])
+        launch_stats = {k: round(st[k], 5) for k in ("min_ms", "median_ms", "p95_ms", "max_ms", "cv_pct")}
+        launch_stats["samples"] = n_s
+        launch_stats["timing"] = "separate pass, CUDA event after every launch (not the value)"
+    except Exception as e:  # diagnostics only: never costs the line
+        log(f"rank {rank}: launch stats unavailable: {e}")
+    for p in plans:
+        rc, st_word = p.status()
+        if rc != 0:
+            raise SystemExit(f"device status {st_word} after the per-launch pass")
+
     # Single-matrix workloads: the same launches captured in one CUDA graph
     # (k launches per replay, device time / k), which removes the host's
     # per-launch cost; reported beside the stream-launched value, not in it.
@@ -614,6 +639,7 @@ def main() -> int:
             "matrices_per_s": round(job_matrices / (ms_step / 1e3), 2),
             "roofline_pct": round(100.0 * value / (peak * world), 2),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "graph": graph,
+            "launch_stats": launch_stats,
             "gather": gather,
             "gpu_launches": args.steps * world, "gpu_launches_per_rank": args.steps,
         }
