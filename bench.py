@@ -1,21 +1,23 @@
 """Benchmark of the B200 fused causal softmax (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c4|c1|c2a|c2b|c3|c5]
+                    [--workload c4|c1|c2a|c2b|c3|c5] [--weak]
 
 Default workload (one step): the batched multi-head configuration, B=8 x H=32
 causal softmaxes of 4096 x 4096 FP16 scores (256 matrices, 8 GiB in, 8 GiB
 out), values half(N(0,1)*3) from seed 3, scale 1/sqrt(128). With N ranks (one
-process per GPU, launched by torchrun for N > 1) every rank runs its own batch
-of 256 independent heads (weak scaling: the job is N x 256 matrices). The
+process per GPU, launched by torchrun for N > 1) the 256 heads are sharded
+evenly: rank k runs matrices [k*256/N, (k+1)*256/N) of the seeded stream
+(strong scaling: the job stays 256 matrices). --weak gives every rank its own
+256 heads instead (the job grows to N x 256; labelled "weak"). The
 single-matrix workloads (c1 4096^2, c2a 1000x1037 pitch 1040, c2b 4096x32, c3
 8192^2 stress, c5 32768^2) shard one matrix over the ranks (strong scaling):
 rank k holds row block [t_k, t_k+1) and its mirror [M - t_k+1, M - t_k) of
 the M rows, stored one after the other (a folded plan: row_offset plus
 cs_plan_set_row_split), so each rank's row pairs are those of the whole
-matrix; --contiguous-rows (and matrices with more rows than columns) use
-contiguous blocks of equal causal cost. There is no collective on the data
-path: ranks meet only at the timing barriers.
+matrix; --contiguous-rows (and matrices with more rows than columns, or too
+few rows to fold) use contiguous blocks of equal causal cost. There is no
+collective on the data path: ranks meet only at the timing barriers.
 
 value  = algorithmic bytes of all ranks per step (triangle read 2*T + full
          write 2*M*N per matrix) / step time, in GB/s; step time is the max
@@ -41,8 +43,10 @@ cpu_baseline = the reference CPU path (C restatement of
             host/examples/cpu_bench.rs) on rank 0 at N=1, on a bounded sample.
 
 --impl reference times that CPU path on all host threads of rank 0 (there is
-no Rust toolchain to build the reference itself), one bounded sample of the
-workload per step.
+no Rust toolchain to build the reference itself): every step runs whole
+matrices of the workload, row-parallel, with inputs from the oracle's copy of
+the seeded generator. That arm loads only the oracle library, never this
+package's CUDA library, and prints the same config as this arm.
 """
 from __future__ import annotations
 
@@ -54,6 +58,8 @@ import statistics
 import sys
 import threading
 import time
+
+import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "gb200-sm100a-tma-fused-causal-attention-softmax_b200")
@@ -67,7 +73,7 @@ WORKLOADS = {
     "c4": dict(config=4, seed=3, matrices=256, rows=4096, cols=4096, pitch=4096, scale=INV_SQRT128,
                shard="heads", values="half(N(0,1)*3)",
                desc="batched multi-head causal softmax, B=8 H=32 L=4096: 256 matrices of "
-                    "4096x4096 FP16 scores per rank"),
+                    "4096x4096 FP16 scores, heads sharded evenly over the ranks"),
     "c1": dict(config=1, seed=0, matrices=1, rows=4096, cols=4096, pitch=4096, scale=INV_SQRT128,
                shard="rows", values="half(N(0,1)*4)",
                desc="single 4096x4096 causal softmax, row blocks sharded over ranks"),
@@ -94,8 +100,6 @@ def log(*a):
 
 
 def f32(x: float) -> float:
-    import numpy as np
-
     return float(np.float32(x))
 
 
@@ -121,19 +125,28 @@ def ncu_traffic_per_matrix(kernel: str, workload: str) -> float | None:
 
 def row_blocks(rows: int, cols: int, parts: int) -> list[tuple[int, int]]:
     """Split rows into `parts` contiguous blocks of equal cost, cost(r) =
-    2*min(r+1, cols) (causal read) + 2*cols (full write)."""
+    2*min(r+1, cols) (causal read) + 2*cols (full write). Needs rows >= parts
+    (every rank gets at least one row)."""
+    if rows < parts:
+        raise ValueError(f"{rows} rows cannot be split over {parts} ranks: every rank needs a row")
     cost = [2 * min(r + 1, cols) + 2 * cols for r in range(rows)]
     total = sum(cost)
     bounds, acc, k = [0], 0, 1
     for r, c in enumerate(cost):
         acc += c
-        if k < parts and acc >= total * k / parts:
+        if k < parts and acc >= total * k / parts and r + 1 <= rows - (parts - k):
             bounds.append(r + 1)
             k += 1
-    while len(bounds) < parts:
-        bounds.append(rows)
+    while len(bounds) < parts:  # keep one row for each remaining rank
+        bounds.append(max(bounds[-1] + 1, rows - (parts - len(bounds))))
     bounds.append(rows)
     return [(bounds[i], bounds[i + 1]) for i in range(parts)]
+
+
+def can_fold(rows: int, cols: int, parts: int) -> bool:
+    """Folded shards need rows <= cols and at least one row per rank in every
+    block and its mirror (rows // 2 >= parts)."""
+    return rows <= cols and rows // 2 >= parts
 
 
 def rank_segments(rows: int, cols: int, parts: int, rank: int, fold: bool = True) -> list[tuple[int, int]]:
@@ -141,18 +154,70 @@ def rank_segments(rows: int, cols: int, parts: int, rank: int, fold: bool = True
     single matrix, in the order they are stored.
 
     Folded (rows <= cols, so every row but possibly the last is shorter than
-    the row width): rank k < parts-1 holds rows [t_k, t_k+1) and their mirror
-    [rows - t_k+1, rows - t_k), t_k = k * (rows // 2) // parts, and the last
-    rank the middle block [t_parts-1, rows - t_parts-1). Each shard's row pairs
-    then carry rows + 1 causal elements, as in the whole matrix, and the
-    shards are equal. Otherwise: contiguous blocks of equal causal cost."""
-    if not fold or rows > cols:
+    the row width, and rows // 2 >= parts): rank k < parts-1 holds rows
+    [t_k, t_k+1) and their mirror [rows - t_k+1, rows - t_k),
+    t_k = k * (rows // 2) // parts, and the last rank the middle block
+    [t_parts-1, rows - t_parts-1). Each shard's row pairs then carry rows + 1
+    causal elements, as in the whole matrix, and the shards are equal.
+    Otherwise (fold off, tall matrices, or too few rows to give every rank a
+    block and its mirror): contiguous blocks of equal causal cost."""
+    if not fold or not can_fold(rows, cols, parts):
         a, b = row_blocks(rows, cols, parts)[rank]
         return [(a, b - a)]
     t = [k * (rows // 2) // parts for k in range(parts)]
     if rank == parts - 1:
         return [(t[rank], rows - 2 * t[rank])]
     return [(t[rank], t[rank + 1] - t[rank]), (rows - t[rank + 1], t[rank + 1] - t[rank])]
+
+
+def head_range(matrices: int, parts: int, rank: int) -> tuple[int, int]:
+    """First matrix and matrix count of one rank's even share of the heads."""
+    if matrices < parts:
+        raise ValueError(f"{matrices} heads cannot be split over {parts} ranks")
+    a, b = rank * matrices // parts, (rank + 1) * matrices // parts
+    return a, b - a
+
+
+def rank_share(w: dict, world: int, rank: int, weak: bool, contiguous: bool):
+    """(first matrix, matrices, row segments, scaling, job matrices) of one rank."""
+    if w["shard"] == "heads":
+        if weak:
+            # Every rank runs its own full batch of independent heads
+            # (matrices rank*M .. rank*M + M - 1 of the seeded stream).
+            return rank * w["matrices"], w["matrices"], [(0, w["rows"])], "weak", w["matrices"] * world
+        first_b, n_local = head_range(w["matrices"], world, rank)
+        return first_b, n_local, [(0, w["rows"])], "strong", w["matrices"]
+    segs = rank_segments(w["rows"], w["cols"], world, rank, fold=not contiguous)
+    return 0, w["matrices"], segs, "strong", w["matrices"]
+
+
+def rotation(w: dict, n_local: int, rows_local: int) -> tuple[int, int, str]:
+    """Buffer sets rotated per launch so that consecutive launches touch more
+    than 2 x L2, the bytes of one set (in + out), and the config's l2 note."""
+    copy_bytes = 2 * n_local * rows_local * w["pitch"] * 2
+    n_rot = 1 if copy_bytes >= 2 * L2_BYTES else math.ceil(2 * L2_BYTES / copy_bytes) + 1
+    note = (f"{n_rot} rotated buffer sets of {copy_bytes / 2**20:.2f} MiB (in+out) per rank"
+            if n_rot > 1 else f"inputs larger than L2 ({copy_bytes / 2**20:.0f} MiB in+out per rank), no flush")
+    return n_rot, copy_bytes, note
+
+
+def job_config(args, w: dict, world: int) -> tuple[dict, str]:
+    """The `config` object of the JSON line and the scaling label. Both arms
+    (this library and --impl reference) print exactly this, computed without
+    loading either implementation."""
+    first_b, n_local, segs, scaling, job_matrices = rank_share(w, world, 0, args.weak,
+                                                               args.contiguous_rows)
+    _, _, l2 = rotation(w, n_local, sum(n for _, n in segs))
+    cfg = {"workload": w["desc"], "name": args.workload, "matrices": job_matrices,
+           "matrices_per_rank": n_local, "rows": w["rows"], "cols": w["cols"], "pitch": w["pitch"],
+           "values": w["values"], "seed": w["seed"], "scale": w["scale"], "kernel": args.kernel,
+           "shard": ("heads, every rank its own full batch (weak)" if scaling == "weak" else
+                     "heads split evenly over the ranks" if w["shard"] == "heads" else
+                     "folded row blocks of one matrix (a block and its mirror per rank)"
+                     if not args.contiguous_rows and can_fold(w["rows"], w["cols"], world) else
+                     "contiguous row blocks of one matrix, equal causal cost"),
+           "l2": l2}
+    return cfg, scaling
 
 
 class ClockSampler:
@@ -221,16 +286,18 @@ def _oracle():
     return oracle_ctypes
 
 
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
 def cpu_sample(w: dict, seconds: float, threads: int) -> dict:
     """Times the reference CPU path on whole matrices of the workload (row
     blocks of at most 4096 rows for the long-context matrix) for ~`seconds`."""
-    import causal_softmax as cs
-
     O = _oracle()
     rows, cols, pitch = w["rows"], w["cols"], w["pitch"]
     blk = min(rows, 4096)
     scale = f32(w["scale"])
-    x = cs.generate(w["config"], w["seed"], batch=1, rows=blk, cols=cols, pitch=pitch)[0].ravel()
+    x = O.generate(w["config"], w["seed"], 1, blk, cols, pitch)[0].ravel()
     O.softmax_strided(x, 1, 0, min(blk, 64), cols, pitch, 0, scale, threads=1)  # warm-up
     done_bytes, done_rows, t0 = 0.0, 0, time.perf_counter()
     while True:
@@ -238,7 +305,7 @@ def cpu_sample(w: dict, seconds: float, threads: int) -> dict:
         off = (done_rows // blk * blk) % rows
         n = min(blk, rows - off)
         O.softmax_strided(x, 1, 0, n, cols, pitch, off, scale, threads=threads)
-        done_bytes += cs.roofline_bytes(n, cols, off)
+        done_bytes += O.roofline_bytes(n, cols, off)
         done_rows += n
         if time.perf_counter() - t0 >= seconds:
             break
@@ -246,47 +313,66 @@ def cpu_sample(w: dict, seconds: float, threads: int) -> dict:
     return {"value": round(done_bytes / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{done_rows} rows ({done_rows / rows:.2f} matrices) of the {w['rows']}x{w['cols']} "
                       f"workload, {threads} thread(s), {dt:.1f} s; "
-                      f"matrices/s = {done_bytes / cs.roofline_bytes(rows, cols) / dt:.4f}"}
+                      f"matrices/s = {done_bytes / O.roofline_bytes(rows, cols) / dt:.4f}"}
 
 
 def run_reference(args, w: dict) -> None:
-    """Reference arm: the CPU path on all host threads of rank 0."""
+    """Reference arm: the reference's CPU path (the oracle's C restatement of
+    reference/src/lib.rs:85-108, kind "port") on all host threads of rank 0.
+    Every step softmaxes whole matrices of the workload, row-parallel; the
+    inputs come from the oracle's copy of the seeded generator. Nothing of
+    this package (its CUDA library included) is loaded."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    import causal_softmax as cs
-
     O = _oracle()
-    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    config, scaling = job_config(args, w, world)
+    threads = host_threads()
     rows, cols, pitch = w["rows"], w["cols"], w["pitch"]
-    # One step = a bounded sample: up to 256 rows per thread of one matrix, row-parallel.
-    n = min(rows, max(256, 256 * threads // max(1, cols // 4096)))
-    off = max(0, rows // 2 - n // 2)
-    x = cs.generate(w["config"], w["seed"], batch=1, rows=n, cols=cols, pitch=pitch, first_row=off)[0]
-    x = x.ravel()
     scale = f32(w["scale"])
+    # A pool of distinct matrices of the workload (the heads stream from seed;
+    # single-matrix workloads have one), cycled step after step.
+    pool_n = min(4, config["matrices"])
+    x = O.generate(w["config"], w["seed"], pool_n, rows, cols, pitch, threads=threads)
+    y = np.empty_like(x[0])
+    mat_bytes = O.roofline_bytes(rows, cols)
+    done = [0]
+
+    def one_matrix():
+        O.softmax_strided(x[done[0] % pool_n].ravel(), 1, 0, rows, cols, pitch, 0, scale,
+                          threads=threads)
+        done[0] += 1
+
+    t0 = time.perf_counter()
+    one_matrix()
+    t_one = time.perf_counter() - t0
+    # Whole matrices per step: enough for ~50 ms of work (one for the large workloads).
+    per_step = max(1, min(64, round(0.05 / max(t_one, 1e-6))))
     for _ in range(args.warmup):
-        O.softmax_strided(x, 1, 0, n, cols, pitch, off, scale, threads=threads)
+        for _ in range(per_step):
+            one_matrix()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.softmax_strided(x, 1, 0, n, cols, pitch, off, scale, threads=threads)
+        for _ in range(per_step):
+            one_matrix()
         times.append(time.perf_counter() - t0)
+    del y
     step = statistics.mean(times)
-    alg = cs.roofline_bytes(n, cols, off)
-    value = alg / step / 1e9
+    value = per_step * mat_bytes / step / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak" if w["shard"] == "heads" else "strong", "vs_baseline": None,
+        "scaling": scaling, "vs_baseline": None,
         "dtype": "f32", "io_dtype": "f16", "data": "synthetic",
-        "config": {"workload": w["desc"], "rows": rows, "cols": cols, "pitch": pitch,
-                   "values": w["values"], "seed": w["seed"], "scale": w["scale"],
-                   "sample_rows_per_step": n, "sample_first_row": off},
-        "matrices_per_s": round(alg / cs.roofline_bytes(rows, cols) / step, 4),
+        "config": config,
+        "matrices_per_s": round(per_step / step, 4),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"rows {off}..{off + n} of one matrix per step, split over "
-                                   f"{threads} threads (C restatement of reference/src/lib.rs:85-108)"},
+                         "sample": f"{per_step} whole {rows}x{cols} matrices per step (a pool of "
+                                   f"{pool_n} seeded matrices, cycled), rows split over {threads} "
+                                   f"threads; C restatement of reference/src/lib.rs:85-108, f32, "
+                                   f"glibc expf, on the host cores of rank 0"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -308,6 +394,8 @@ def main() -> int:
                     help="N > 1: skip the separately reported gather of all outputs to rank 0")
     ap.add_argument("--contiguous-rows", action="store_true",
                     help="single matrices: contiguous row blocks instead of folded shards")
+    ap.add_argument("--weak", action="store_true",
+                    help="batched workload: every rank runs its own full batch (weak scaling)")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the CUDA-graph timing of the single-matrix workloads")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -327,7 +415,6 @@ def main() -> int:
         run_reference(args, w)
         return 0
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -350,19 +437,13 @@ def main() -> int:
 
     rows_full, cols, pitch = w["rows"], w["cols"], w["pitch"]
     scale = f32(w["scale"])
-    if w["shard"] == "heads":
-        # Weak scaling: every rank runs its own batch of independent heads
-        # (matrices rank*M .. rank*M + M - 1 of the seeded stream); there is
-        # no exchange between ranks on this path.
-        n_local, first_b = w["matrices"], rank * w["matrices"]
-        segs = [(0, rows_full)]
-        scaling, job_matrices = "weak", w["matrices"] * world
-    else:
-        # Strong scaling: the rows of one matrix, as a folded shard (a row
-        # block and its mirror, stored one after the other) or one block.
-        n_local, first_b = w["matrices"], 0
-        segs = rank_segments(rows_full, cols, world, rank, fold=not args.contiguous_rows)
-        scaling, job_matrices = "strong", w["matrices"]
+    # Heads split evenly over the ranks (or, with --weak, a full batch per
+    # rank); single matrices as folded row-block shards (a block and its
+    # mirror, stored one after the other) or contiguous blocks. No exchange
+    # between ranks on this path.
+    first_b, n_local, segs, scaling, job_matrices = rank_share(w, world, rank, args.weak,
+                                                               args.contiguous_rows)
+    config, _ = job_config(args, w, world)
     rows = sum(n for _, n in segs)
     r0 = segs[0][0]
 
@@ -375,8 +456,7 @@ def main() -> int:
         cs.generate(w["config"], w["seed"], batch=n_local, rows=n, cols=cols, pitch=pitch,
                     first_batch=first_b, first_row=a, out=h_in.numpy().view(np.uint16)[:, off:off + n])
         off += n
-    copy_bytes = 2 * h_in.numel() * 2
-    n_rot = 1 if copy_bytes >= 2 * L2_BYTES else math.ceil(2 * L2_BYTES / copy_bytes) + 1
+    n_rot, copy_bytes, _ = rotation(w, n_local, rows)
     d_in = [h_in.cuda().view(torch.float16) for _ in range(n_rot)]
     d_out = [torch.empty_like(d_in[0]) for _ in range(n_rot)]
     seg_text = " + ".join(f"{a}..{a + n}" for a, n in segs)
@@ -624,18 +704,12 @@ def main() -> int:
         cpu = cpu_sample(w, args.cpu_seconds, 1)
 
     if rank == 0:
-        l2 = (f"{n_rot} rotated buffer sets of {copy_bytes / 2**20:.0f} MiB (in+out) per rank"
-              if n_rot > 1 else f"inputs larger than L2 ({copy_bytes / 2**20:.0f} MiB in+out per rank), no flush")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "io_dtype": "f16", "data": "synthetic",
-            "config": {"workload": w["desc"], "name": args.workload, "matrices": job_matrices,
-                       "matrices_per_rank": n_local,
-                       "rows": rows_full, "cols": cols, "pitch": pitch, "values": w["values"],
-                       "seed": w["seed"], "scale": w["scale"], "kernel": info["kernel_name"],
-                       "l2": l2},
+            "config": config,
             "matrices_per_s": round(job_matrices / (ms_step / 1e3), 2),
             "roofline_pct": round(100.0 * value / (peak * world), 2),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "graph": graph,

@@ -29,7 +29,7 @@ OK = 0
 ERR = {
     -1: "EMPTY", -2: "WRONG_LENGTH", -3: "BAD_SCALE", -4: "NON_FINITE", -5: "WARP_COLS",
     -6: "ALIGNMENT", -7: "PITCH", -8: "BAD_KERNEL", -9: "DEVICE", -10: "CUDA", -11: "TIMEOUT",
-    -12: "NULL", -13: "PADDING", -14: "UNSUPPORTED", -15: "PROBE", -16: "ARG",
+    -12: "NULL", -13: "PADDING", -14: "UNSUPPORTED", -15: "PROBE", -16: "ARG", -17: "STATUS",
 }
 ERR_CODE = {v: k for k, v in ERR.items()}
 STATUS_TIMEOUT = 1
@@ -126,6 +126,7 @@ def _declare(L) -> None:
         "cs_padded_pitch": (c_i64, [c_i64]),
         "cs_validate": (c_int, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32]),
         "cs_check_finite_host": (c_int, [u16p, c_i64]),
+        "cs_status_error": (c_int, [ctypes.c_uint32]),
         "cs_plan_create": (c_int, [ctypes.POINTER(vp), c_int, vp, vp, c_i64, c_i64, c_i32, c_i32,
                                    c_i32, c_i32]),
         "cs_plan_launch": (c_int, [vp, c_int, c_f32, vp]),
@@ -141,6 +142,7 @@ def _declare(L) -> None:
                                        c_f32, vp]),
         "cs_softmax_noalloc": (c_int, [c_int, vp, vp, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32,
                                        c_f32, c_i32, ctypes.POINTER(ctypes.c_uint32), vp]),
+        "cs_noalloc_status": (c_int, [c_i32, ctypes.POINTER(ctypes.c_uint32), vp]),
         "cs_session_create": (c_int, [ctypes.POINTER(vp), c_int]),
         "cs_session_probe": (c_int, [vp]),
         "cs_session_softmax_host": (c_int, [vp, c_int, u16p, u16p, c_i64, c_i32, c_i32, c_i32,

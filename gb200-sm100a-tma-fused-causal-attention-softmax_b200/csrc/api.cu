@@ -826,6 +826,7 @@ const char* cs_strerror(int code) {
     case CS_ERR_UNSUPPORTED: return "shape not supported by the selected kernel";
     case CS_ERR_PROBE: return "probe kernel mismatch";
     case CS_ERR_ARG: return "invalid argument";
+    case CS_ERR_STATUS: return "device status word holds reserved bits";
     default: return "unknown error code";
   }
 }
@@ -905,6 +906,13 @@ int cs_check_finite_host(const uint16_t* scores, int64_t n) {
   for (int64_t i = 0; i < n; ++i)
     if ((scores[i] & 0x7c00u) == 0x7c00u) return CS_ERR_NON_FINITE;
   return CS_OK;
+}
+
+int cs_status_error(uint32_t status) {
+  if (status == 0) return CS_OK;
+  if (status & CS_STATUS_TIMEOUT) return CS_ERR_TIMEOUT;
+  std::snprintf(t_detail, sizeof t_detail, "device status word 0x%08x: reserved bits set", status);
+  return CS_ERR_STATUS;
 }
 
 int cs_device_sm_count(int device) {
@@ -1029,7 +1037,7 @@ int cs_plan_status(cs_plan* plan, uint32_t* status) {
   CS_CUDA(cudaMemcpy(&s, plan->d_status, sizeof s, cudaMemcpyDeviceToHost));
   CS_CUDA(cudaMemset(plan->d_status, 0, sizeof s));
   if (status) *status = s;
-  return (s & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
+  return cs_status_error(s);
 }
 
 int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
@@ -1172,7 +1180,29 @@ int cs_softmax_noalloc(int kernel, const void* d_in, void* d_out, int64_t batch,
   CS_CUDA(cudaMemcpyAsync(&word, words + slot, sizeof word, cudaMemcpyDeviceToHost, s));
   CS_CUDA(cudaStreamSynchronize(s));
   *status = word;
-  return (word & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
+  return cs_status_error(word);
+}
+
+int cs_noalloc_status(int32_t slot, uint32_t* status, void* stream) {
+  if (!status) return CS_ERR_NULL;
+  if (slot < 0 || slot >= CS_NOALLOC_SLOTS) {
+    std::snprintf(t_detail, sizeof t_detail,
+                  "status slot %d out of range: the static status array holds %d words (slots 0..%d)",
+                  (int)slot, CS_NOALLOC_SLOTS, CS_NOALLOC_SLOTS - 1);
+    return CS_ERR_ARG;
+  }
+  int dev = 0;
+  CS_CUDA(cudaGetDevice(&dev));
+  uint32_t* words = nullptr;
+  const int rc = noalloc_status_for(dev, &words);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t word = 0;
+  CS_CUDA(cudaMemcpyAsync(&word, words + slot, sizeof word, cudaMemcpyDeviceToHost, s));
+  CS_CUDA(cudaMemsetAsync(words + slot, 0, sizeof(uint32_t), s));
+  CS_CUDA(cudaStreamSynchronize(s));
+  *status = word;
+  return cs_status_error(word);
 }
 
 // ===========================================================================
@@ -1228,7 +1258,7 @@ static int session_read_status(cs_session* s) {
   uint32_t st = 0;
   CS_CUDA(cudaMemcpy(&st, s->d_status, sizeof st, cudaMemcpyDeviceToHost));
   if (st) CS_CUDA(cudaMemset(s->d_status, 0, sizeof st));
-  return (st & CS_STATUS_TIMEOUT) ? CS_ERR_TIMEOUT : CS_OK;
+  return cs_status_error(st);
 }
 
 int64_t cs_host_copy_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t row_offset) {

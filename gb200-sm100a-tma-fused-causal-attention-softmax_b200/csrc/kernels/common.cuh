@@ -11,9 +11,9 @@
 
 namespace cs {
 
-// Device status bits (written with atomicOr into the plan's status word).
+// Device status bit (written with atomicOr into the plan's status word); the
+// other bits of the word are reserved and never set.
 constexpr uint32_t kStatusTimeout = 1u;   // a bounded mbarrier wait ran out
-constexpr uint32_t kStatusBadUnit = 2u;   // a work unit decoded out of range
 
 // Debug flags a launch may carry (test-only code paths, off by default).
 constexpr uint32_t kFlagSkipLoads = 1u;   // producer issues no copies: waits must time out

@@ -71,14 +71,16 @@ enum {
     CS_ERR_PADDING = -13,       /* nonzero padded output found */
     CS_ERR_UNSUPPORTED = -14,   /* shape beyond the selected kernel's limits */
     CS_ERR_PROBE = -15,         /* probe kernel returned a wrong value */
-    CS_ERR_ARG = -16            /* other invalid argument */
+    CS_ERR_ARG = -16,           /* other invalid argument */
+    CS_ERR_STATUS = -17         /* device status word holds bits no kernel defines */
 };
 
 #define CS_MAX_SCALE 1.0e30f   /* reference/src/lib.rs:5 */
 
-/* Device status word bits reported by cs_plan_status. */
+/* Device status word bits reported by cs_plan_status (and the session and
+ * no-alloc status reads). A kernel sets only CS_STATUS_TIMEOUT: a bounded
+ * device-side wait ran out. Every other bit is reserved. */
 #define CS_STATUS_TIMEOUT 1u
-#define CS_STATUS_BAD_UNIT 2u
 
 /* ---------------------------------------------------------------- */
 /* Host-only queries (no GPU needed)                                 */
@@ -135,6 +137,12 @@ int cs_validate(int64_t batch, int64_t batch_stride, int64_t rows, int64_t cols,
  * NaN or infinite, else CS_OK. */
 int cs_check_finite_host(const uint16_t *scores, int64_t n);
 
+/* The error code a device status word maps to, as every status read in this
+ * library reports it (the reference propagates device failures as errors,
+ * gpu/src/driver.rs:108-211): CS_OK for 0, CS_ERR_TIMEOUT when
+ * CS_STATUS_TIMEOUT is set, CS_ERR_STATUS for any other (reserved) bit. */
+int cs_status_error(uint32_t status);
+
 /* ---------------------------------------------------------------- */
 /* Device path: plans (replaces gpu/src/driver.rs:65-211)            */
 /* ---------------------------------------------------------------- */
@@ -162,8 +170,7 @@ int cs_plan_create(cs_plan **plan, int device, const void *d_in, void *d_out, in
 int cs_plan_launch(cs_plan *plan, int kernel, float scale, void *stream);
 
 /* Synchronise the plan's device and read (then clear) its status word.
- * *status receives the CS_STATUS_* bits; returns CS_ERR_TIMEOUT if the
- * timeout bit was set, CS_OK otherwise. */
+ * *status receives the CS_STATUS_* bits; returns cs_status_error of them. */
 int cs_plan_status(cs_plan *plan, uint32_t *status);
 
 /* Bound, in nanoseconds of GPU time, on every device-side wait of later
@@ -243,8 +250,9 @@ int cs_softmax_batched(int kernel, const void *d_in, void *d_out, int64_t batch,
  * same slot race on it: one call's clear can erase the other's timeout bit.
  * Callers that launch on several streams at once give each stream its own
  * slot. If `status` is non-null the call waits for `stream`, stores the
- * CS_STATUS_* bits there and returns CS_ERR_TIMEOUT if a bounded wait ran
- * out; if it is null the call returns after the launch.
+ * CS_STATUS_* bits there and returns cs_status_error of them; if it is null
+ * the call returns after the launch, and the slot's word can be read later
+ * with cs_noalloc_status.
  *
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress, which may load the library's device code); make that
@@ -255,6 +263,16 @@ int cs_softmax_noalloc(int kernel, const void *d_in, void *d_out, int64_t batch,
                        int64_t batch_stride, int32_t rows, int32_t cols, int32_t pitch,
                        int32_t row_offset, float scale, int32_t slot, uint32_t *status,
                        void *stream);
+
+/* No counterpart in the reference. Reads, then clears, the status word of
+ * no-alloc slot `slot` on the current device, for callers that passed a null
+ * `status` to cs_softmax_noalloc and synchronise on their own terms: the copy
+ * and the clear are ordered on `stream` after the launches issued there, and
+ * the call waits for `stream` before it stores the bits in *status. Allocates
+ * nothing. Returns cs_status_error of the bits, CS_ERR_ARG for a bad slot,
+ * CS_ERR_NULL for a null `status`. A later launch on the same slot clears the
+ * word itself, so read it before reusing the slot. */
+int cs_noalloc_status(int32_t slot, uint32_t *status, void *stream);
 
 /* ---------------------------------------------------------------- */
 /* Sessions: host buffers (replaces gpu/src/driver.rs:12-59, 213-248) */

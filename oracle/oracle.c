@@ -429,3 +429,113 @@ int or_accept_strided(const uint16_t *got, const uint16_t *f64_ref, int64_t batc
     if (report) *report = r;
     return (r.mask_violations || r.elem_violations || r.rowsum_violations) ? 1 : 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* Benchmark workload generator (synthetic stand-in for a dataset)      */
+/* ------------------------------------------------------------------ */
+
+/* Vigna's splitmix64 finaliser (public-domain published algorithm). */
+static inline uint64_t gen_mix(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+/* Box-Muller on two 24-bit uniforms of one hash; the first is in (0, 1]. */
+static inline double gen_normal(uint64_t h) {
+    const double u1 = (double)((h >> 40) + 1) * (1.0 / 16777216.0);
+    const double u2 = (double)((h >> 16) & 0xFFFFFFu) * (1.0 / 16777216.0);
+    return sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+}
+
+typedef struct {
+    uint16_t *out;
+    int config;
+    uint64_t seed;
+    int64_t stride, rows, cols, pitch, first_batch, first_row, begin, end;
+} gen_job;
+
+static void *gen_worker(void *arg) {
+    const gen_job *j = (const gen_job *)arg;
+    for (int64_t t = j->begin; t < j->end; ++t) {
+        const int64_t b = t / j->rows, r = t % j->rows, a = j->first_row + r;
+        uint16_t *y = j->out + b * j->stride + r * j->pitch;
+        const uint64_t key =
+            gen_mix(gen_mix(j->seed + 0x632BE59BD9B4E019ull * (uint64_t)(j->first_batch + b)) + (uint64_t)a);
+        for (int64_t c = 0; c < j->cols; ++c) {
+            const uint64_t h = gen_mix(key + (uint64_t)c);
+            double v;
+            if (j->config == 1) {
+                v = gen_normal(h) * 4.0;
+            } else if (j->config == 2) {
+                v = -8.0 + 16.0 * ((double)(h >> 11) * (1.0 / 9007199254740992.0));
+            } else if (j->config == 3) {
+                const uint64_t h2 = gen_mix(h ^ 0xD1B54A32D192ED03ull);
+                v = (h2 % 100 == 0) ? (((h2 >> 32) & 1u) ? 60000.0 : -60000.0) : gen_normal(h) * 8.0;
+            } else if (j->config == 4) {
+                v = gen_normal(h) * 3.0;
+            } else {
+                v = gen_normal(h) * 2.0 + 0.001 * (double)c;
+            }
+            y[c] = or_f32_to_half((float)v);
+        }
+        for (int64_t c = j->cols; c < j->pitch; ++c) y[c] = 0;
+        if (j->config == 3 && a >= 1) {
+            /* Two more copies of the row's causal maximum at distinct columns. */
+            const int64_t valid = (a + 1) < j->cols ? (a + 1) : j->cols;
+            if (valid >= 2) {
+                int64_t arg = 0;
+                float best = or_half_to_f32(y[0]);
+                for (int64_t c = 1; c < valid; ++c) {
+                    const float f = or_half_to_f32(y[c]);
+                    if (f > best) {
+                        best = f;
+                        arg = c;
+                    }
+                }
+                const uint16_t mbits = y[arg];
+                const uint64_t hk = gen_mix(key ^ 0x8CB92BA72F3D8DD7ull);
+                const int64_t c1 = (int64_t)(hk % (uint64_t)valid);
+                const int64_t c2 = (c1 + 1 + (int64_t)((hk >> 32) % (uint64_t)(valid - 1))) % valid;
+                y[c1] = mbits;
+                y[c2] = mbits;
+            }
+        }
+    }
+    return NULL;
+}
+
+int or_generate(uint16_t *out, int config, uint64_t seed, int64_t batch, int64_t batch_stride,
+                int64_t rows, int64_t cols, int64_t pitch, int64_t first_batch,
+                int64_t first_row, int threads) {
+    if (!out || config < 1 || config > 5) return OR_WRONG_LENGTH;
+    if (batch <= 0 || rows <= 0 || cols <= 0) return OR_EMPTY;
+    if (pitch < cols || first_row < 0 || first_batch < 0) return OR_WRONG_LENGTH;
+    if (batch > 1 && batch_stride < rows * pitch) return OR_WRONG_LENGTH;
+    const int64_t total = batch * rows;
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if ((int64_t)threads > total) threads = (int)total;
+    gen_job jobs[256];
+    pthread_t tids[256];
+    const int64_t per = (total + threads - 1) / threads;
+    for (int k = 0; k < threads; ++k) {
+        jobs[k] = (gen_job){out, config, seed, batch > 1 ? batch_stride : rows * pitch, rows, cols,
+                            pitch, first_batch, first_row, (int64_t)k * per,
+                            ((int64_t)k + 1) * per < total ? ((int64_t)k + 1) * per : total};
+        tids[k] = 0;
+    }
+    if (threads == 1) {
+        gen_worker(&jobs[0]);
+        return OR_OK;
+    }
+    for (int k = 0; k < threads; ++k)
+        if (pthread_create(&tids[k], NULL, gen_worker, &jobs[k]) != 0) {
+            gen_worker(&jobs[k]); /* run inline if a thread cannot start */
+            tids[k] = 0;
+        }
+    for (int k = 0; k < threads; ++k)
+        if (tids[k]) pthread_join(tids[k], NULL);
+    return OR_OK;
+}

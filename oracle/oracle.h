@@ -126,6 +126,22 @@ int or_accept_strided(const uint16_t *got, const uint16_t *f64_ref, int64_t batc
                       int64_t row_offset, double abs_tol, int64_t ulp_tol, double rowsum_tol,
                       or_accept_report *report);
 
+/*
+ * Seeded synthetic score matrices of the benchmark workloads (the reference
+ * publishes no dataset; these stand in for it). Restated here so the bench's
+ * CPU leg and the tests can build inputs without the product library; the
+ * tests check it bit for bit against the library's cs_generate.
+ *   element (matrix b, absolute row r, column c): h = splitmix64(key(seed, b, r) + c),
+ *   key(seed, b, r) = splitmix64(splitmix64(seed + K*b) + r);
+ *   config 1: half(N(0,1)*4); 2: half(U(-8,8)); 3: half(N(0,1)*8) with 1% of entries
+ *   +-60000 and two planted copies of each row's causal maximum; 4: half(N(0,1)*3);
+ *   5: half(N(0,1)*2 + 0.001*c). N(0,1) by Box-Muller on 24-bit uniforms.
+ * Pitch padding is written 0. Rows are split over `threads` POSIX threads.
+ */
+int or_generate(uint16_t *out, int config, uint64_t seed, int64_t batch, int64_t batch_stride,
+                int64_t rows, int64_t cols, int64_t pitch, int64_t first_batch,
+                int64_t first_row, int threads);
+
 #ifdef __cplusplus
 }
 #endif

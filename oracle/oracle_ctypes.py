@@ -93,6 +93,8 @@ def lib():
             L.or_accept_strided.argtypes = [u16p, u16p, i64, i64, i64, i64, i64, i64,
                                             ctypes.c_double, i64, ctypes.c_double,
                                             ctypes.POINTER(AcceptReport)]
+            L.or_generate.argtypes = [u16p, ctypes.c_int, ctypes.c_uint64, i64, i64, i64, i64, i64,
+                                      i64, i64, ctypes.c_int]
             _lib = L
     return _lib
 
@@ -183,6 +185,36 @@ def softmax_strided(inp: np.ndarray, batch: int, batch_stride: int, rows: int, c
     if rc != OK:
         raise ValueError(f"oracle rejected the shape (code {rc})")
     return out
+
+
+def generate(config: int, seed: int, batch: int, rows: int, cols: int, pitch: int | None = None,
+             first_batch: int = 0, first_row: int = 0, threads: int = 0,
+             out: np.ndarray | None = None) -> np.ndarray:
+    """Seeded workload matrices (oracle.h or_generate): uint16 half bits of shape
+    (batch, rows, pitch), written into `out` when given."""
+    pitch = padded_pitch(cols) if pitch is None else pitch
+    if out is None:
+        out = np.empty((batch, rows, pitch), dtype=np.uint16)
+    if out.dtype != np.uint16 or out.size != batch * rows * pitch:
+        raise ValueError("out must be uint16 of batch*rows*pitch elements")
+    if not out.flags.c_contiguous:
+        raise ValueError("out must be contiguous")
+    if threads <= 0:
+        threads = os.cpu_count() or 1
+    rc = lib().or_generate(_p(out), config, seed, batch, rows * pitch, rows, cols, pitch,
+                           first_batch, first_row, threads)
+    if rc != OK:
+        raise ValueError(f"oracle generator rejected the shape (code {rc})")
+    return out
+
+
+def roofline_bytes(rows: int, cols: int, row_offset: int = 0) -> float:
+    """Algorithmic bytes of one matrix: 2*T (causal prefix read) + 2*rows*cols
+    (full write), T = causal elements of rows [row_offset, row_offset+rows)
+    (host/src/lib.rs:52-56 for row_offset 0)."""
+    tri = max(0, min(rows, cols - 1 - row_offset))
+    t = tri * (row_offset + 1) + tri * (tri - 1) // 2 + (rows - tri) * cols
+    return 2.0 * t + 2.0 * rows * cols
 
 
 def verify(got, expected, rows: int, cols: int, len_override: tuple | None = None):

@@ -56,6 +56,24 @@ def test_strerror_and_kernel_names():
     assert L.cs_kernel_name(99) is None
 
 
+def test_status_word_mapping():
+    # Every status read (plan, session, no-alloc) maps the device word through
+    # cs_status_error: kernels only ever set the timeout bit; any other bit is
+    # reserved and reported as CS_ERR_STATUS rather than silently ignored.
+    L = cs.lib()
+    E = cs.ERR_CODE
+    assert L.cs_status_error(0) == cs.OK
+    assert L.cs_status_error(cs.STATUS_TIMEOUT) == E["TIMEOUT"]
+    assert L.cs_status_error(cs.STATUS_TIMEOUT | 0x80000000) == E["TIMEOUT"]
+    for word in (2, 4, 0x100, 0x80000000, 0xFFFFFFFE):
+        assert L.cs_status_error(word) == E["STATUS"], hex(word)
+        assert b"reserved bits" in L.cs_last_error_detail()
+    assert L.cs_strerror(E["STATUS"]).decode() == "device status word holds reserved bits"
+    # No header bit besides the timeout: the library defines no other status.
+    text = open(cs.HEADER_PATHS[0]).read()
+    assert re.findall(r"#define (CS_STATUS_\w+)", text) == ["CS_STATUS_TIMEOUT"]
+
+
 def test_supports_and_auto_dispatch():
     L = cs.lib()
     # host/src/lib.rs:43-45, 461-470

@@ -54,11 +54,11 @@ def _worker(rank: int, world: int, port: int, q):
                              for (s0, n), o in zip(segs, np.cumsum([0] + [n for _, n in segs]))])
         fparts = [None] * world
         dist.all_gather_object(fparts, yf)
-        # Heads (the batched workload).
+        # Heads (the batched workload), split as bench.py splits them.
         heads, hr = 6, 40
         hp = cs.padded_pitch(hr)
-        per = heads // world
-        xh = cs.generate(4, 3, batch=per, rows=hr, cols=hr, first_batch=rank * per)
+        first, per = bench.head_range(heads, world, rank)
+        xh = cs.generate(4, 3, batch=per, rows=hr, cols=hr, first_batch=first)
         yh = O.softmax_strided(xh.ravel(), per, hr * hp, hr, hr, hp, 0, 0.0883883).reshape(per, hr, hp)
         hparts = [None] * world
         dist.all_gather_object(hparts, yh)
@@ -121,13 +121,56 @@ def test_row_blocks_balance_causal_cost():
     import bench
 
     for rows, cols, parts in [(4096, 4096, 2), (4096, 4096, 8), (32768, 32768, 8), (1000, 1037, 4),
-                              (4096, 32, 8), (7, 100, 8)]:
+                              (4096, 32, 8), (8, 100, 8), (9, 100, 8), (3, 3, 2)]:
         blocks = bench.row_blocks(rows, cols, parts)
         assert len(blocks) == parts and blocks[0][0] == 0 and blocks[-1][1] == rows
-        assert all(b[0] <= b[1] for b in blocks)
+        assert all(b[0] < b[1] for b in blocks), (rows, cols, parts, blocks)  # no empty shard
         assert all(blocks[i][1] == blocks[i + 1][0] for i in range(parts - 1))
         cost = lambda a, b: sum(2 * min(r + 1, cols) + 2 * cols for r in range(a, b))
         costs = [cost(a, b) for a, b in blocks]
         row_cost = 2 * cols + 2 * min(rows, cols)
         if rows >= 8 * parts:
             assert max(costs) - min(costs) <= 2 * row_cost, (rows, cols, parts, costs)
+
+
+def test_shards_never_empty_and_fold_falls_back():
+    import bench
+
+    # Fewer rows than ranks: a clear error instead of empty shards.
+    with pytest.raises(ValueError, match="every rank needs a row"):
+        bench.row_blocks(7, 100, 8)
+    # Too few rows to give every rank a block and its mirror: contiguous blocks.
+    for rows, cols, parts in [(8, 100, 8), (15, 100, 8), (3, 3, 2)]:
+        assert not bench.can_fold(rows, cols, parts)
+        segs = [bench.rank_segments(rows, cols, parts, r) for r in range(parts)]
+        assert all(len(s) == 1 and s[0][1] > 0 for s in segs), segs
+        assert sum(s[0][1] for s in segs) == rows
+    # Enough rows: folded, every segment non-empty, all rows covered once.
+    for rows, cols, parts in [(16, 100, 8), (4096, 4096, 8), (301, 320, 2), (32768, 32768, 8)]:
+        assert bench.can_fold(rows, cols, parts)
+        seen = np.zeros(rows, np.int32)
+        for r in range(parts):
+            for a, n in bench.rank_segments(rows, cols, parts, r):
+                assert n > 0
+                seen[a:a + n] += 1
+        assert np.all(seen == 1)
+
+
+def test_head_split_matches_job():
+    import bench
+
+    for heads, world in [(256, 1), (256, 2), (256, 4), (256, 8), (6, 4), (7, 3)]:
+        ranges = [bench.head_range(heads, world, r) for r in range(world)]
+        assert sum(n for _, n in ranges) == heads
+        assert all(ranges[r][0] + ranges[r][1] == ranges[r + 1][0] for r in range(world - 1))
+        assert max(n for _, n in ranges) - min(n for _, n in ranges) <= 1
+    with pytest.raises(ValueError):
+        bench.head_range(2, 4, 0)
+    # The batched workload: strong scaling keeps the job at 256 heads, N = 1
+    # is the whole batch, and --weak gives every rank its own 256.
+    w = bench.WORKLOADS["c4"]
+    for world in (1, 2, 4, 8):
+        first, n, segs, scaling, job = bench.rank_share(w, world, world - 1, False, False)
+        assert (scaling, job, n, first) == ("strong", 256, 256 // world, 256 - 256 // world)
+        first, n, segs, scaling, job = bench.rank_share(w, world, world - 1, True, False)
+        assert (scaling, job, n, first) == ("weak", 256 * world, 256, 256 * (world - 1))
