@@ -134,6 +134,7 @@ def _declare(L) -> None:
         "cs_plan_set_timeout": (c_int, [vp, ctypes.c_uint64]),
         "cs_plan_set_row_split": (c_int, [vp, c_i32, c_i32]),
         "cs_plan_set_tuning": (c_int, [vp, c_int, c_int, c_int, c_int]),
+        "cs_plan_set_prefetch": (c_int, [vp, c_int]),
         "cs_plan_describe": (c_int, [vp, c_int, ctypes.POINTER(LaunchInfo)]),
         "cs_plan_launch_debug": (c_int, [vp, c_int, c_f32, vp, ctypes.c_uint32, ctypes.c_uint64]),
         "cs_plan_destroy": (None, [vp]),
@@ -281,6 +282,9 @@ class Plan:
                    zero_fill_tma: int = -1) -> None:
         check(lib().cs_plan_set_tuning(self._h, vec, stages, l2_hint, zero_fill_tma),
               "cs_plan_set_tuning")
+
+    def set_prefetch(self, prefetch_units: int = -1) -> None:
+        check(lib().cs_plan_set_prefetch(self._h, prefetch_units), "cs_plan_set_prefetch")
 
     def describe(self, kernel="auto") -> dict:
         info = LaunchInfo()

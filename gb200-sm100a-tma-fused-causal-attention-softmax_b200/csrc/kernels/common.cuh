@@ -136,6 +136,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// Bulk prefetch of `bytes` (multiple of 16) at global `src` (16-byte aligned)
+// into L2; no data reaches the SM and nothing completes on a barrier.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // 1-D TMA bulk store shared -> global, tracked by the bulk async-group.
 __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),

@@ -52,13 +52,17 @@ struct RowResParams {
   int32_t stage_bytes;  // bytes per stage (multiple of 128, >= 16 * max vectors per unit)
   int32_t l2_hint;      // 1: evict-first L2 hint on the input copies
   int32_t zero_tma;     // 1: masked columns by bulk stores, 0: by consumer stores
+  int32_t prefetch;     // static units per CTA whose rows are pulled into L2 before the previous kernel ends
 };
 
 // Shared memory after the stages: zero buffer, 2 x 32 float2 (max, sum)
-// partials, full and empty mbarriers per stage, abort flag, and the unit each
-// stage holds (-1: no more units).
+// partials, full and empty mbarriers per stage, abort flag, the unit each
+// stage holds as its consumers see it (-1: no more units), and the
+// producer's record of each stage's unit (matrix, in-matrix index) for its
+// bulk stores -- in shared memory rather than a per-thread array, so that no
+// kernel needs local memory.
 __host__ __device__ constexpr int rowres_tail_bytes(int stages) {
-  return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16 + ((4 * stages + 15) / 16) * 16;
+  return kZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16 + 3 * (((4 * stages + 15) / 16) * 16);
 }
 
 // Shared-memory-resident consumers (V == 0), for rows too long to hold in
@@ -234,11 +238,16 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
   const int32_t G = gridDim.x;
   const int32_t first = blockIdx.x;
   const int32_t total = (int32_t)p.m.total_units;
-  const int32_t n_mine = first < total ? (total - 1 - first) / G + 1 : 0;
   const int32_t upm = p.m.units_per_matrix;
   const int32_t gq = G / upm, gr = G - (G / upm) * upm;
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
   const int32_t pv = g.pitch >> 3;  // 16-byte vectors per output row
+  const int32_t n_mine = first < total ? (total - 1 - first) / G + 1 : 0;
+  // Only the shared-memory consumers read unit ids, so only they can follow claims.
+  const bool claims = V == 0 && g.sched != nullptr;
+  // Static units of this CTA (the rest, if any, are claimed).
+  const int32_t n_static_mine = claims ? min(S, n_mine) : n_mine;
+  const bool has_claims = claims && (int64_t)S * G < total;
 
   for (int i = tid; i < kZeroBytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(zero_buf)[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -253,211 +262,199 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
   }
   __syncthreads();
   pdl_trigger();
-  pdl_wait();  // inputs written, outputs read by the previous kernel: done
 
   if (warp == W) {
     // ------------------------------------------------------------ producer
     if (lane != 0 || skip_loads) return;
-    const uint64_t policy = p.l2_hint ? policy_evict_first() : 0ull;
+    const bool name_all = V == 0;  // consumers that read every stage's unit id
+    // Unit held by each stage: matrix and in-matrix index (for its bulk stores).
+    int32_t* sb = const_cast<int32_t*>(unit_id) + ((S + 3) & ~3);
+    int32_t* sk = sb + ((S + 3) & ~3);
+    // One unit's rows and 16-byte vector counts (computed once per unit).
+    struct UnitGeo {
+      int32_t b, kk, ra, rb;
+      uint32_t na, nb;
+    };
+    auto geo = [&](int32_t b, int32_t kk) {
+      UnitGeo u;
+      u.b = b;
+      u.kk = kk;
+      unit_rows(p.m, kk, u.ra, u.rb);
+      u.na = (uint32_t)(valid_cols(g, u.ra) + 7) >> 3;
+      u.nb = u.rb >= 0 ? (uint32_t)(valid_cols(g, u.rb) + 7) >> 3 : 0u;
+      return u;
+    };
+    // The static sequence first, first + G, ... as (matrix, in-matrix index)
+    // cursors stepped without division.
+    auto step = [&](int32_t& b, int32_t& kk) {
+      kk += gr;
+      b += gq;
+      if (kk >= upm) {
+        kk -= upm;
+        ++b;
+      }
+    };
+    // Masked columns and pitch padding of a unit: bulk stores from the zero buffer.
+    auto zero_fill = [&](const UnitGeo& u) {
+      uint16_t* out_m = g.out + (int64_t)u.b * g.batch_stride;
+      for (int r = 0; r < 2; ++r) {
+        const int32_t row = r == 0 ? u.ra : u.rb;
+        if (row < 0) break;
+        const uint32_t nv = r == 0 ? u.na : u.nb;
+        uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)nv * 8);
+        uint32_t left = (uint32_t)(pv - (int32_t)nv) * 16u;
+        while (left) {
+          const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
+          bulk_s2g(z, zero_buf, n);
+          z += n;
+          left -= n;
+        }
+      }
+      bulk_commit();
+      bulk_wait_read_16();
+    };
     // kTmaStore: the output of the unit that last used a stage is stored
     // from it before the stage is refilled.
     auto store_unit = [&](int32_t ub, int32_t uk, int s) {
-      int32_t ra, rb;
-      unit_rows(p.m, uk, ra, rb);
-      const uint32_t na = (uint32_t)(valid_cols(g, ra) + 7) >> 3;
-      const uint32_t nb = rb >= 0 ? (uint32_t)(valid_cols(g, rb) + 7) >> 3 : 0u;
+      const UnitGeo u = geo(ub, uk);
       uint16_t* out_m = g.out + (int64_t)ub * g.batch_stride;
       const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
-      bulk_s2g(out_m + (int64_t)ra * g.pitch, st, na * 16u);
-      if (nb) bulk_s2g(out_m + (int64_t)rb * g.pitch, st + (size_t)na * 16, nb * 16u);
+      bulk_s2g(out_m + (int64_t)u.ra * g.pitch, st, u.na * 16u);
+      if (u.nb) bulk_s2g(out_m + (int64_t)u.rb * g.pitch, st + (size_t)u.na * 16, u.nb * 16u);
       bulk_commit();
     };
-    int32_t sb[24], sk[24];  // unit held by each stage (kTmaStore)
-    if constexpr (V == 0) {
-      // Shared-memory consumers read each stage's unit from unit_id; units
-      // past the first S per CTA may be claimed at run time (g.sched).
-      bool aborted = false;
-      int32_t issued = 0;
-      // The unit of the next iteration: a static index, or a claim issued after
-      // this iteration's copies (its L2 round trip overlaps them).
-      int64_t next = first;
-      int32_t k = 0;
-      for (;; ++k) {
-        const int s = k % S;
-        if (k >= S) {
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
-            aborted = true;
-            *abort_flag = 1;
-            if (g.status) atomicOr(g.status, kStatusTimeout);
-            break;
-          }
-          if (kTmaStore) {
-            store_unit(sb[s], sk[s], s);
-            bulk_wait_read_all();  // the stage is read out before it is refilled
-          }
-        }
-        if (next >= total) {
-          unit_id[s] = -1;  // consumers that read unit ids stop here
-          mbar_arrive(&full[s]);
+    // Stage s receives unit u: its transaction bytes are announced first
+    // (possibly before the previous kernel has finished), its copies are
+    // issued only after that kernel has.
+    auto announce = [&](const UnitGeo& u, int s) { mbar_arrive_expect_tx(&full[s], (u.na + u.nb) * 16u); };
+    auto load = [&](const UnitGeo& u, int s) {
+      uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+      const uint16_t* src = g.in + (int64_t)u.b * g.batch_stride;
+      if (p.l2_hint) {
+        const uint64_t policy = policy_evict_first();
+        bulk_g2s_hint(dst, src + (int64_t)u.ra * g.pitch, u.na * 16u, &full[s], policy);
+        if (u.nb) bulk_g2s_hint(dst + u.na * 16u, src + (int64_t)u.rb * g.pitch, u.nb * 16u, &full[s], policy);
+      } else {
+        bulk_g2s(dst, src + (int64_t)u.ra * g.pitch, u.na * 16u, &full[s]);
+        if (u.nb) bulk_g2s(dst + u.na * 16u, src + (int64_t)u.rb * g.pitch, u.nb * 16u, &full[s]);
+      }
+    };
+
+    int32_t lb = first / upm, lkk = first - (first / upm) * upm;  // next static unit to load
+    // The first min(S, n_static_mine) units are static: announce them and
+    // start pulling their rows into L2 before waiting for the previous kernel
+    // (a prefetch consumes no data, and L2 is where every write lands, so
+    // nothing stale can be read), then issue their copies at once.
+    const int32_t n_pre = min(S, n_static_mine);
+    for (int32_t k = 0; k < n_pre; ++k) {
+      if (name_all) unit_id[k] = first + k * G;
+      const UnitGeo u = geo(lb, lkk);
+      announce(u, k);
+      const uint16_t* src = g.in + (int64_t)u.b * g.batch_stride;
+      bulk_prefetch_l2(src + (int64_t)u.ra * g.pitch, u.na * 16u);
+      if (u.nb) bulk_prefetch_l2(src + (int64_t)u.rb * g.pitch, u.nb * 16u);
+      sb[k] = lb;
+      sk[k] = lkk;
+      step(lb, lkk);
+    }
+    {
+      // More of this CTA's static units, into L2 only.
+      int32_t pb = lb, pk = lkk;
+      for (int32_t k = n_pre; k < min(p.prefetch, n_static_mine); ++k) {
+        const UnitGeo u = geo(pb, pk);
+        const uint16_t* src = g.in + (int64_t)u.b * g.batch_stride;
+        bulk_prefetch_l2(src + (int64_t)u.ra * g.pitch, u.na * 16u);
+        if (u.nb) bulk_prefetch_l2(src + (int64_t)u.rb * g.pitch, u.nb * 16u);
+        step(pb, pk);
+      }
+    }
+    pdl_wait();  // inputs written, outputs read by the previous kernel: done
+    for (int32_t k = 0; k < n_pre; ++k) {
+      const UnitGeo u = geo(sb[k], sk[k]);
+      load(u, k);
+      if (p.zero_tma) zero_fill(u);
+    }
+
+    bool aborted = false;
+    int32_t k = n_pre;  // also the number of units whose copies were issued, at every exit below
+    // Units past the static part are claimed one iteration ahead, after that
+    // iteration's copies, so the claim's L2 round trip overlaps them.
+    auto claim = [&]() -> int32_t {
+      const int64_t u = (int64_t)S * G + atomicAdd(&g.sched[0], 1u);
+      return u < total ? (int32_t)u : -1;
+    };
+    int32_t next = k < n_static_mine ? 0 : (has_claims ? claim() : -1);  // the claimed unit, -1: none
+    for (;; ++k) {
+      const int s = k % S;
+      if (k >= S) {
+        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
+          aborted = true;
+          *abort_flag = 1;
+          if (g.status) atomicOr(g.status, kStatusTimeout);
           break;
         }
-        const int32_t u = (int32_t)next;
-        unit_id[s] = u;
-        const int32_t b = u / upm, kk = u - (u / upm) * upm;
-        int32_t ra, rb;
-        unit_rows(p.m, kk, ra, rb);
-        const int32_t va = valid_cols(g, ra);
-        const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
-        const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
-        uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
-        const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
-        mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
-        if (p.l2_hint) {
-          bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
-          if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
-        } else {
-          bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
-          if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
-        }
-        ++issued;
-        if (p.zero_tma) {
-          uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
-          for (int r = 0; r < 2; ++r) {
-            const int32_t row = r == 0 ? ra : rb;
-            if (row < 0) break;
-            uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
-            uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
-            while (left) {
-              const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
-              bulk_s2g(z, zero_buf, n);
-              z += n;
-              left -= n;
-            }
-          }
-          bulk_commit();
-          bulk_wait_read_16();
-        }
         if (kTmaStore) {
-          sb[s] = b;
-          sk[s] = kk;
-        }
-        if (k + 1 < S || g.sched == nullptr)
-          next = (int64_t)first + (int64_t)(k + 1) * G;
-        else
-          next = (int64_t)S * G + atomicAdd(&g.sched[0], 1u);
-      }
-      if (kTmaStore && !aborted) {
-        // Outputs of the units still held by the other stages (iteration k
-        // stored the one before it in its own stage).
-        for (int32_t j = k + 1; j < k + S; ++j) {
-          if (j - S < 0) continue;
-          const int s = j % S;
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((j / S) - 1) & 1), g.timeout_ns)) {
-            if (g.status) atomicOr(g.status, kStatusTimeout);
-            break;
-          }
           store_unit(sb[s], sk[s], s);
+          bulk_wait_read_all();  // the stage is read out before it is refilled
         }
       }
-      if (g.sched != nullptr) {
-        // The last CTA to finish claiming resets the counters for the next launch.
-        __threadfence();
-        if (atomicAdd(&g.sched[1], 1u) == (uint32_t)G - 1) {
-          atomicExch(&g.sched[0], 0u);
-          atomicExch(&g.sched[1], 0u);
+      const bool is_static = k < n_static_mine;
+      if (!is_static && next < 0) {
+        // End mark for the consumers that read unit ids.
+        if (name_all) {
+          unit_id[s] = -1;
+          mbar_arrive(&full[s]);
         }
+        break;
       }
-      bulk_wait_all();
-      // After an abort: copies this warp issued that no consumer waited for.
-      // (Without one, every copy was consumed, and the stage that received the
-      // end mark has completed one more phase, so its parity no longer tells.)
-      if (aborted)
-        for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
-          (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
-    } else {
-      // Register-resident consumers follow the static schedule with their own
-      // cursor; this producer steps the same cursor.
-      int32_t b = first / upm, kk = first - (first / upm) * upm;
-      bool aborted = false;
-      int32_t issued = 0;
-      for (int32_t k = 0; k < n_mine; ++k) {
-        const int s = k % S;
-        if (k >= S) {
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
-            aborted = true;
-            *abort_flag = 1;
-            if (g.status) atomicOr(g.status, kStatusTimeout);
-            break;
-          }
-          if (kTmaStore) {
-            store_unit(sb[s], sk[s], s);
-            bulk_wait_read_all();  // the stage is read out before it is refilled
-          }
-        }
-        int32_t ra, rb;
-        unit_rows(p.m, kk, ra, rb);
-        const int32_t va = valid_cols(g, ra);
-        const int32_t vb = rb >= 0 ? valid_cols(g, rb) : 0;
-        const uint32_t na = (uint32_t)(va + 7) >> 3, nb = (uint32_t)(vb + 7) >> 3;
-        uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
-        const uint16_t* src = g.in + (int64_t)b * g.batch_stride;
-        mbar_arrive_expect_tx(&full[s], (na + nb) * 16u);
-        if (p.l2_hint) {
-          bulk_g2s_hint(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s], policy);
-          if (nb) bulk_g2s_hint(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s], policy);
-        } else {
-          bulk_g2s(dst, src + (int64_t)ra * g.pitch, na * 16u, &full[s]);
-          if (nb) bulk_g2s(dst + na * 16u, src + (int64_t)rb * g.pitch, nb * 16u, &full[s]);
-        }
-        ++issued;
-        if (p.zero_tma) {
-          uint16_t* out_m = g.out + (int64_t)b * g.batch_stride;
-          for (int r = 0; r < 2; ++r) {
-            const int32_t row = r == 0 ? ra : rb;
-            if (row < 0) break;
-            uint8_t* z = reinterpret_cast<uint8_t*>(out_m + (int64_t)row * g.pitch + (int64_t)(r == 0 ? na : nb) * 8);
-            uint32_t left = (uint32_t)(pv - (int32_t)(r == 0 ? na : nb)) * 16u;
-            while (left) {
-              const uint32_t n = left < (uint32_t)kZeroBytes ? left : (uint32_t)kZeroBytes;
-              bulk_s2g(z, zero_buf, n);
-              z += n;
-              left -= n;
-            }
-          }
-          bulk_commit();
-          bulk_wait_read_16();
-        }
-        if (kTmaStore) {
-          sb[s] = b;
-          sk[s] = kk;
-        }
-        kk += gr;
-        b += gq;
-        if (kk >= upm) {
-          kk -= upm;
-          ++b;
-        }
+      UnitGeo u;
+      if (is_static) {
+        u = geo(lb, lkk);
+        step(lb, lkk);
+        if (name_all) unit_id[s] = first + k * G;
+      } else {
+        u = geo(next / upm, next - (next / upm) * upm);
+        unit_id[s] = next;
       }
-      if (kTmaStore && !aborted) {
-        // Outputs of the last min(S, n_mine) units.
-        for (int32_t k = n_mine; k < n_mine + S && k - S < n_mine; ++k) {
-          if (k < S) continue;
-          const int s = k % S;
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((k / S) - 1) & 1), g.timeout_ns)) {
-            if (g.status) atomicOr(g.status, kStatusTimeout);
-            break;
-          }
-          store_unit(sb[s], sk[s], s);
-        }
-      }
-      bulk_wait_all();
-      // Copies this warp issued that no consumer waited for (after an abort).
-      for (int32_t r = (issued > S ? issued - S : 0); r < issued; ++r)
-        (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+      announce(u, s);
+      load(u, s);
+      if (p.zero_tma) zero_fill(u);
+      sb[s] = u.b;
+      sk[s] = u.kk;
+      if (k + 1 >= n_static_mine) next = has_claims ? claim() : -1;
     }
+    if (kTmaStore && !aborted) {
+      // Outputs of the units still held by the other stages (iteration k
+      // stored the one before it in its own stage).
+      for (int32_t j = k + 1; j < k + S; ++j) {
+        if (j - S < 0) continue;
+        const int s = j % S;
+        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((j / S) - 1) & 1), g.timeout_ns)) {
+          if (g.status) atomicOr(g.status, kStatusTimeout);
+          break;
+        }
+        store_unit(sb[s], sk[s], s);
+      }
+    }
+    if (claims) {
+      // The last CTA to finish claiming resets the counters for the next launch.
+      __threadfence();
+      if (atomicAdd(&g.sched[1], 1u) == (uint32_t)G - 1) {
+        atomicExch(&g.sched[0], 0u);
+        atomicExch(&g.sched[1], 0u);
+      }
+    }
+    bulk_wait_all();
+    // After an abort: copies this warp issued that no consumer waited for.
+    // (Without one, every copy was consumed, and a stage that received the
+    // end mark has completed one more phase, so its parity no longer tells.)
+    if (aborted)
+      for (int32_t r = (k > S ? k - S : 0); r < k; ++r)
+        (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
     return;
   }
 
+  pdl_wait();  // consumers store to global memory (outputs, thread zero-fill)
   // -------------------------------------------------------------- consumers
   if constexpr (V == 0) {
     rowres_pass_consumers<kTmaStore>(p, stage_base, red, full, empty, abort_flag, unit_id, warp, lane, W);

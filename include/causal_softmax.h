@@ -197,6 +197,14 @@ int cs_plan_set_row_split(cs_plan *plan, int32_t split_row, int32_t split_offset
 int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint,
                        int zero_fill_tma);
 
+/* TMA / PIPELINE kernels: the input rows of the first `prefetch_units` work
+ * units of each CTA (row pairs; -1 = automatic, 0..1024, never fewer than
+ * the ring's first stages) are pulled into L2 while the previous kernel in
+ * the stream is still finishing, before the launch waits for it (a
+ * prefetch consumes no data). Affects later launches of the plan; one-shot
+ * launches (cs_softmax*) use the automatic depth. */
+int cs_plan_set_prefetch(cs_plan *plan, int prefetch_units);
+
 typedef struct cs_launch_info {
     int32_t kernel;          /* resolved cs_kernel */
     int32_t grid;            /* CTAs per launch */

@@ -384,6 +384,88 @@ def test_repeated_launches_are_fast_and_exact(cols):
         check(from_dev(d_out), x, cols=cols, scale=0.125, what=f"repeated {kernel} {rows}x{cols}")
 
 
+@pytest.mark.parametrize("variant", [None, 1, 5, 6, 7])
+def test_l2_prefetch_depth_changes_no_bit(variant):
+    # The row-resident kernel pulls the rows of each CTA's first units into
+    # L2 before it waits for the previous kernel: whatever the depth, the
+    # launch reads its inputs after that wait, so the output bits are those
+    # of the shallowest prefetch, for consecutive launches of one plan whose
+    # input the previous kernel in the stream has just rewritten.
+    for rows, cols, batch, off in [(4096, 4096, 1, 0), (700, 700, 3, 0), (301, 5000, 2, 4000)]:
+        x = cs.generate(2, 9, batch=batch, rows=rows, cols=cols, first_row=off)
+        d_in = to_dev(x)
+        outs = []
+        for depth in (0, 3, 4, 64):
+            d_out = sentinel_like(d_in)
+            with cs.Plan.for_tensors(d_in, d_out, cols=cols, row_offset=off) as plan:
+                if variant is not None:
+                    try:
+                        plan.set_tuning(16 + variant, 0, -1, -1)
+                        plan.describe("pipeline")
+                    except cs.CausalSoftmaxError as e:
+                        assert e.code == cs.ERR_CODE["UNSUPPORTED"], e
+                        break
+                plan.set_prefetch(depth)
+                for _ in range(2):
+                    d_in.view(torch.int16).bitwise_not_()  # the input changes right before the launch
+                    plan.launch("pipeline", 0.0883883)
+                assert plan.status() == (0, 0)
+            outs.append(from_dev(d_out))
+        if not outs:
+            continue
+        what = f"variant {variant} {batch}x{rows}x{cols}+{off}"
+        for b in range(batch):
+            check(outs[0][b], x[b], cols=cols, scale=0.0883883, row_offset=off, what=what)
+        for o in outs[1:]:
+            assert np.array_equal(o, outs[0]), what
+
+
+def test_chained_launches_read_the_previous_output():
+    # Launch B reads what launch A (just before it on the stream) writes.
+    # B starts while A finishes (programmatic dependent launch) and prefetches
+    # its input rows into L2 before it waits for A; its loads come after the
+    # wait, so B must see A's final output: softmax applied twice, with the
+    # same bits as two launches separated by a device synchronisation.
+    for rows, cols, kernel, tuning in [(4096, 4096, "pipeline", None), (2048, 2048, "tma", None),
+                                       (1000, 1037, "pipeline", (23, 0, -1, -1)), (600, 20000, "auto", None)]:
+        pitch = cs.padded_pitch(cols)
+        x = cs.generate(1, 12, batch=1, rows=rows, cols=cols, pitch=pitch)[0]
+        d_in = to_dev(x)
+        mids = [sentinel_like(d_in) for _ in range(2)]
+        outs = [sentinel_like(d_in) for _ in range(2)]
+        for i, chained in enumerate((True, False)):
+            with cs.Plan.for_tensors(d_in, mids[i], cols=cols) as a, \
+                    cs.Plan.for_tensors(mids[i], outs[i], cols=cols) as b:
+                for p in (a, b):
+                    if tuning:
+                        p.set_tuning(*tuning)
+                    p.set_prefetch(64)
+                for _ in range(3):
+                    a.launch(kernel, 0.5)
+                    if not chained:
+                        torch.cuda.synchronize()
+                    b.launch(kernel, 0.5)
+                    if not chained:
+                        torch.cuda.synchronize()
+                assert a.status() == (0, 0) and b.status() == (0, 0)
+        got, want = from_dev(outs[0]), from_dev(outs[1])
+        assert np.array_equal(got, want), (rows, cols, kernel, int(np.count_nonzero(got != want)))
+        check(from_dev(mids[0]), x, cols=cols, scale=0.5, what=f"chained first pass {rows}x{cols}")
+
+
+def test_prefetch_arguments():
+    E = cs.ERR_CODE
+    d_in = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
+    d_out = torch.zeros_like(d_in)
+    L = cs.lib()
+    with cs.Plan.for_tensors(d_in, d_out, cols=64) as plan:
+        assert L.cs_plan_set_prefetch(plan._h, -2) == E["ARG"]
+        assert L.cs_plan_set_prefetch(plan._h, 1025) == E["ARG"]
+        assert L.cs_plan_set_prefetch(None, 1) == E["NULL"]
+        assert L.cs_plan_set_prefetch(plan._h, -1) == 0
+        assert L.cs_plan_set_prefetch(plan._h, 1024) == 0
+
+
 def test_unpaired_fallback_when_a_pair_does_not_fit():
     # Forcing 2 vectors per thread caps a unit at 30 warps x 64 vectors: row
     # pairs of ~24000 columns do not fit, single rows (~1500 vectors) do, so
