@@ -280,10 +280,20 @@ bool rowres_shape(int64_t max_nv, bool paired, int want_vec) {
 // Variant groups in order of preference: V = 4 first, then the
 // shared-memory passes (V = 0), then V = 8 and V = 2, which only a tuning
 // request reaches. Measured on B200 over square widths 1024..32768: V = 4
-// wins wherever it fits (up to ~12000 columns; 6108 GB/s at 12288 against
-// 6027 for V = 0); beyond, V = 0 beats V = 8 by 7-36% (16384^2: 5509 against
-// 4655 GB/s; 32768^2: 526 against 714 us).
+// wins wherever it fits for single matrices (up to ~12000 columns: 4096^2
+// 12.3 against 16.0 us, 8192^2 36.2 against 37.4 us, 12288^2 76.5 against
+// 79.8 us); beyond, V = 0 beats V = 8 by 7-36% (16384^2: 5509 against 4655
+// GB/s; 32768^2: 526 against 714 us). In steady state (many units per CTA,
+// see kSteadyUnitsPerCta) V = 0 keeps more CTAs resident and wins instead,
+// except near 4096 columns, where four V = 4 CTAs fill an SM: batched
+// launches of ~2 GB, V = 0 against V = 4, GB/s: 2048 cols 4889/4381, 3072
+// 5613/5327, 4096 5698/5827, 5120 5957/5847, 6144 6448/6108, 7168 6422/5830,
+// 8192 6528/6013, 10240 6499/5464, 12288 6106/6191.
 constexpr int kRowGroups[4][3] = {{4, 6, 2}, {7, -1, -1}, {0, 1, -1}, {5, 3, -1}};
+constexpr int64_t kSteadyUnitsPerCta = 32;
+// Widest units (16-byte vectors) of the band where V = 4 stays ahead in
+// steady state: rows of ~3600 to ~4600 columns.
+constexpr int64_t kV4BandLo = 450, kV4BandHi = 578;
 
 // Pick the variant for units of up to max_nv vectors. Within a group the
 // score is resident warps per SM x registers^1.5: more resident warps hide
@@ -327,6 +337,20 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
     const int rc = rowres_pick(d, max_nv, m.n_pairs > 0, t.vec, stage_bytes, tma_store, &variant, &block);
     if (rc == CS_OK) break;
     if (rc != CS_ERR_UNSUPPORTED) return rc;
+  }
+  if (variant >= 0 && t.vec == 0 && kRowVariants[variant].vec != 0 && (max_nv < kV4BandLo || max_nv > kV4BandHi)) {
+    // Steady state: the shared-memory variant, if every CTA of its grid gets
+    // at least kSteadyUnitsPerCta units.
+    int v0 = -1, b0 = 0;
+    if (rowres_pick(d, max_nv, m.n_pairs > 0, 16 + 7, stage_bytes, tma_store, &v0, &b0) == CS_OK) {
+      int per_sm0 = 0;
+      CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm0, rowres_kernel_ptr(v0, tma_store), b0,
+                                                            2 * stage_bytes + cs::rowres_tail_bytes(2)));
+      if (per_sm0 > 0 && m.total_units >= kSteadyUnitsPerCta * (int64_t)d.sms * per_sm0) {
+        variant = v0;
+        block = b0;
+      }
+    }
   }
   const int vec = variant >= 0 ? kRowVariants[variant].vec : 0;
   if (variant < 0) {

@@ -51,6 +51,8 @@ class AcceptReport(ctypes.Structure):
         ("max_ulp", ctypes.c_int64),
         ("max_rowsum_err", ctypes.c_double),
         ("oracle_max_rowsum_err", ctypes.c_double),
+        ("floor_rows", ctypes.c_int64),
+        ("max_floor_excess", ctypes.c_double),
     ]
 
     def as_dict(self) -> dict:
@@ -91,7 +93,7 @@ def lib():
             L.or_causal_softmax_f64_strided.argtypes = strided
             L.or_verify.argtypes = [u16p, u16p, sz, sz, sz, sz, ctypes.POINTER(Accuracy)]
             L.or_accept_strided.argtypes = [u16p, u16p, i64, i64, i64, i64, i64, i64,
-                                            ctypes.c_double, i64, ctypes.c_double,
+                                            ctypes.c_double, i64, ctypes.c_double, ctypes.c_double,
                                             ctypes.POINTER(AcceptReport)]
             L.or_generate.argtypes = [u16p, ctypes.c_int, ctypes.c_uint64, i64, i64, i64, i64, i64,
                                       i64, i64, ctypes.c_int]
@@ -230,13 +232,16 @@ def verify(got, expected, rows: int, cols: int, len_override: tuple | None = Non
 
 def accept(got: np.ndarray, f64_ref: np.ndarray, batch: int, batch_stride: int, rows: int,
            cols: int, pitch: int, row_offset: int, abs_tol: float = 2e-3, ulp_tol: int = 2,
-           rowsum_tol: float = 2e-3) -> dict:
+           rowsum_tol: float = 2e-3, floor_margin: float = -1.0) -> dict:
     """North-star acceptance: masked == 0x0000, unmasked within ulp_tol FP16 ulp or
-    abs_tol absolute of the FP64 oracle, |row sum - 1| <= rowsum_tol."""
+    abs_tol absolute of the FP64 oracle, |row sum - 1| <= rowsum_tol (or, with
+    floor_margin >= 0, within the FP64 oracle's own FP16 row-sum error plus
+    floor_margin on rows where that error already exceeds rowsum_tol)."""
     g, r = _u16(got), _u16(f64_ref)
     rep = AcceptReport()
     rc = lib().or_accept_strided(_p(g), _p(r), batch, batch_stride, rows, cols, pitch,
-                                 row_offset, abs_tol, ulp_tol, rowsum_tol, ctypes.byref(rep))
+                                 row_offset, abs_tol, ulp_tol, rowsum_tol, floor_margin,
+                                 ctypes.byref(rep))
     d = rep.as_dict()
     d["ok"] = rc == 0
     return d

@@ -37,3 +37,22 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Rows whose row sum was accepted through the FP64 oracle's own FP16
+    rounding error (gpu_helpers.FLOOR_LOG), per checked case."""
+    mod = sys.modules.get("gpu_helpers")
+    if mod is None or not hasattr(mod, "FLOOR_LOG"):
+        return
+    log = mod.FLOOR_LOG
+    tr = terminalreporter
+    tr.write_sep("-", f"row sums accepted through the oracle's own error: {len(log)} case(s)")
+    if not log:
+        return
+    worst = max(e["max_excess"] for e in log)
+    tr.write_line(f"largest excess over the exactly rounded result: {worst:.3g} "
+                  f"(allowed {mod.ROWSUM_FLOOR_MARGIN:g})")
+    for e in log:
+        tr.write_line(f"  {e['what']}: {e['rows']} of {e['checked']} rows, excess <= "
+                      f"{e['max_excess']:.3g}, oracle's own error up to {e['oracle_max_rowsum_err']:.3g}")

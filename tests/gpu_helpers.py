@@ -2,12 +2,18 @@
 with torch (plumbing only), launch through the C ABI, and compare against the
 CPU oracle. Test infrastructure.
 
-Tolerances (checked against the FP64 oracle rounded to
+Tolerances (the north star, checked against the FP64 oracle rounded to
 half): masked entries bit-exact 0x0000; unmasked within ULP_TOL FP16 ulp or
-ABS_TOL absolute; |row sum - 1| <= ROWSUM_TOL. The f32 specification
-(reference/src/lib.rs:85-108) is held to the same element bound, and the
-reference's own verifier (host/src/lib.rs:280-328: 0.003 + 0.003*w per element,
-0.02 per row sum, non-negative, finite, masked == 0) must accept the output.
+ABS_TOL absolute; |row sum - 1| <= ROWSUM_TOL. A row whose exactly rounded
+FP64 result already misses ROWSUM_TOL (FP16 rounding of many small
+probabilities, e.g. uniform rows of ~70000+ columns) may miss it by that much
+(ROWSUM_FLOOR_MARGIN = 0: no worse than exact rounding); every such row is
+recorded in FLOOR_LOG and counted at the end of the test session. No case of
+the suite has needed it on a B200. The f32
+specification (reference/src/lib.rs:85-108) is held to the same element
+bound, and the reference's own verifier (host/src/lib.rs:280-328: 0.003 +
+0.003*w per element, 0.02 per row sum, non-negative, finite, masked == 0)
+must accept the output.
 """
 from __future__ import annotations
 
@@ -20,6 +26,8 @@ import oracle_ctypes as O
 ABS_TOL = 2e-3
 ULP_TOL = 2
 ROWSUM_TOL = 2e-3
+ROWSUM_FLOOR_MARGIN = 0.0
+FLOOR_LOG: list[dict] = []
 SENTINEL = 0xFB00  # gpu/src/driver.rs:78-79
 
 KERNELS = ["baseline", "warp", "tma", "pipeline", "online"]
@@ -73,15 +81,11 @@ def check(got: np.ndarray, x: np.ndarray, *, cols: int, scale: float, row_offset
     ref64 = O.softmax_strided(flat_x, batch, rows * pitch, rows, cols, pitch, row_offset, scale,
                               f64=True)
     rep = O.accept(flat_g, ref64, batch, rows * pitch, rows, cols, pitch, row_offset,
-                   ABS_TOL, ULP_TOL, ROWSUM_TOL)
-    if not rep["ok"] and rep["rowsum_violations"] and not rep["mask_violations"] \
-            and not rep["elem_violations"]:
-        # Row-sum misses the FP64 oracle's own FP16 rounding makes as well are
-        # not kernel errors: allow the oracle's error plus the element slack.
-        rep2 = O.accept(flat_g, ref64, batch, rows * pitch, rows, cols, pitch, row_offset,
-                        ABS_TOL, ULP_TOL, max(ROWSUM_TOL, rep["oracle_max_rowsum_err"] + 1e-3))
-        rep["ok"] = rep2["ok"]
-        rep["rowsum_floor"] = rep["oracle_max_rowsum_err"]
+                   ABS_TOL, ULP_TOL, ROWSUM_TOL, ROWSUM_FLOOR_MARGIN)
+    if rep["floor_rows"]:
+        FLOOR_LOG.append({"what": what, "rows": rep["floor_rows"], "checked": rep["checked_rows"],
+                          "max_excess": rep["max_floor_excess"],
+                          "oracle_max_rowsum_err": rep["oracle_max_rowsum_err"]})
     assert rep["ok"], f"{what}: FP64 acceptance failed {rep}"
     spec = O.softmax_strided(flat_x, batch, rows * pitch, rows, cols, pitch, row_offset, scale)
     rep32 = O.accept(flat_g, spec, batch, rows * pitch, rows, cols, pitch, row_offset,

@@ -166,13 +166,15 @@ def test_config4_batched_multihead():
         assert plan.status() == (0, 0)
     rep = gpu_structure(d_out, L)
     assert rep["mask"] == 0 and rep["values"] == 0 and rep["max_rowsum_err"] <= 2e-3, rep
-    # Full oracle check on three matrices, and batch invariance (a single-matrix
+    # Full oracle check on 32 matrices spread over the batch (every 8th, from
+    # both ends), and batch invariance on three of them (a single-matrix
     # launch gives the same bits as that matrix inside the batched launch).
-    for b in (0, 137, 255):
+    for b in sorted(set(range(0, batch, 8)) | {batch - 1}):
         xb = x[b].numpy().view(np.uint16)
         gb = from_dev(d_out[b])
         check(gb, xb, cols=L, scale=scale, what=f"C4 matrix {b}")
-        assert np.array_equal(run("auto", xb, cols=L, scale=scale), gb)
+        if b in (0, 136, 255):
+            assert np.array_equal(run("auto", xb, cols=L, scale=scale), gb)
 
 
 def test_config5_long_context():
@@ -191,10 +193,10 @@ def test_config5_long_context():
         rep = gpu_structure(d_out, L)
         assert rep["mask"] == 0 and rep["values"] == 0 and rep["max_rowsum_err"] <= 2e-3, rep
         got = from_dev(d_out)
-        # Oracle on row blocks across the matrix (first, middle, last, pair partners).
-        for r0, n in ((0, 64), (8190, 4), (16380, 8), (24570, 4), (L - 64, 64)):
-            check(got[r0:r0 + n], x[r0:r0 + n], cols=L, scale=scale, row_offset=r0,
-                  what=f"C5 {kernel} rows {r0}+{n}")
+        # Every row against the FP64 oracle, in blocks of 2048 rows.
+        for r0 in range(0, L, 2048):
+            check(got[r0:r0 + 2048], x[r0:r0 + 2048], cols=L, scale=scale, row_offset=r0,
+                  what=f"C5 {kernel} rows {r0}+2048")
         del d_out
         torch.cuda.empty_cache()
 

@@ -290,3 +290,43 @@ def test_acceptance_detects_planted_mistakes():
     bad[10 * cols + 3] = O.h(O.f(bad[10 * cols + 3]) + 0.01)
     rep = O.accept(bad, ref, 1, 0, rows, cols, cols, 0)
     assert rep["elem_violations"] == 1 and rep["rowsum_violations"] == 1
+
+
+def test_row_sum_floor_is_per_row_and_bounded():
+    # A uniform row of n columns: every probability is 1/n rounded to FP16.
+    # For n near 2^24 / (k + 1/2) the rounding error of each element is close
+    # to half an ulp in the same direction, so the exactly rounded FP64 result
+    # itself misses the 2e-3 row-sum bound. Such a row is accepted at its own
+    # error plus the margin, and only there; a row whose oracle meets the
+    # bound gets no allowance. Mistakes are planted in the oracle output.
+    best = None
+    for n in range(70000, 140000, 7):
+        h = O.h64(1.0 / n)
+        err = abs(n * O.f(h) - 1.0)
+        if best is None or err > best[1]:
+            best = (n, err)
+    n, err = best
+    assert err > 2.5e-3, best
+    zeros = np.zeros(n, np.uint16)
+    ref = O.softmax_strided(zeros, 1, 0, 1, n, n, n - 1, 0.0, f64=True)
+    assert np.all(ref == O.h64(1.0 / n))
+    # The oracle's own output: fails without an allowance, passes with one.
+    assert not O.accept(ref, ref, 1, 0, 1, n, n, n - 1)["ok"]
+    rep = O.accept(ref, ref, 1, 0, 1, n, n, n - 1, floor_margin=0.0)
+    assert rep["ok"] and rep["floor_rows"] == 1 and rep["max_floor_excess"] == 0.0
+    # One more ulp on 20 elements, away from 1: excess of 20 ulp.
+    worse = ref.copy()
+    step = 1 if n * O.f(ref[0]) > 1.0 else -1
+    worse[:20] = (worse[:20].astype(np.int32) + step).astype(np.uint16)
+    excess = 20 * abs(O.f(worse[0]) - O.f(ref[0]))
+    assert O.accept(worse, ref, 1, 0, 1, n, n, n - 1, floor_margin=2 * excess)["ok"]
+    rep = O.accept(worse, ref, 1, 0, 1, n, n, n - 1, floor_margin=excess / 2)
+    assert not rep["ok"] and rep["rowsum_violations"] == 1
+    # A row whose oracle meets the bound: no allowance at all.
+    m = 4096
+    x = hv(np.linspace(-2, 2, m))
+    r2 = O.softmax_strided(x, 1, 0, 1, m, m, m - 1, 1.0, f64=True)
+    bad = r2.copy()
+    bad[-1] = O.h(O.f(bad[-1]) + 0.004)  # row sum off by ~4e-3, element beyond tolerance too
+    rep = O.accept(bad, r2, 1, 0, 1, m, m, m - 1, floor_margin=1.0)
+    assert not rep["ok"] and rep["floor_rows"] == 0 and rep["rowsum_violations"] == 1
