@@ -34,9 +34,10 @@ BUDGETS = [
     (r"rowres_kernel<4, 224, 4, [01]>", 72, 128,
      "auto's choice for ~3000-5000-column rows: four CTAs per SM cap it at 72 registers; "
      "its few spilled bytes cost ~1% of the instructions (ncu), the occupancy is worth more"),
-    (r"rowres_kernel<8, 576, 1, [01]>", 96, 640,
-     "V = 8 at up to 18 warps; only a tuning request selects it since the shared-memory "
+    (r"rowres_kernel<8, 448, 1, [01]>", 128, 0,
+     "V = 8 at up to 14 warps; only a tuning request selects it since the shared-memory "
      "variant (V = 0) serves long rows"),
+    (r"online_kernel<[12]>", 64, 0, "launch bounds of 1024 threads (the long-row shape)"),
     (r"rowres_kernel<8, 256, 1, [01]>", 168, 0, "V = 8 at up to 8 warps; tuning request only"),
     (r"rowres_kernel<0, 1024, 1, [01]>", 64, 0, "shared-memory passes, 32 warps in one CTA"),
 ]
@@ -54,6 +55,9 @@ def readable(mangled: str) -> str:
     m = re.search(r"narrow_kernelILi(\d+)E", mangled)
     if m:
         return f"narrow_kernel<{m.group(1)}>"
+    m = re.search(r"online_kernelILi(\d+)E", mangled)
+    if m:
+        return f"online_kernel<{m.group(1)}>"
     m = re.search(r"_ZN2cs\d+(\w+?)E", mangled)
     return m.group(1) if m else mangled
 

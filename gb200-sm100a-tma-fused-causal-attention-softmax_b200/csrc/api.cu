@@ -36,6 +36,7 @@ constexpr int kDefaultStages = 3;
 constexpr int64_t kRingBytesPerSm = 72 * 1024;  // row-resident ring bytes per SM (target)
 constexpr int kMaxAutoStages = 8;
 constexpr int kOnlineDefaultStages = 8;
+constexpr int kMaxStages = 32;  // ring depth a tuning request may ask for (shared memory decides the rest)
 constexpr int kOnlineLongRowStages = 4;
 constexpr int64_t kI32Max = 2147483647;
 constexpr int64_t kMaxUnitsPerLaunch = int64_t(1) << 30;  // row-resident kernel, 32-bit unit index
@@ -152,7 +153,9 @@ int device_info(int dev, DeviceInfo** out) {
         CS_CUDA(cudaFuncGetAttributes(&fa, rowres_kernel_ptr(v, ts != 0)));
         d.row_regs[ts][v] = fa.numRegs;
       }
-    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel),
+    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel<1>),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel<2>),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     // Every other kernel a launch may pick, so that the driver has all of the
     // library's code in place once this set-up is done (it may take device
@@ -431,32 +434,48 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
   return CS_OK;
 }
 
+// Online kernel launch shapes: 256 threads x 2 vectors (8 KB tiles), the
+// automatic choice, or -- by tuning request (vec 1) -- 1024 threads x 1
+// vector (16 KB tiles), which holds rows of up to ~114K columns resident on
+// one CTA per SM. Measured on B200 (GB/s): 100000-column rows 2539 for the
+// wide shape against 2858 for two fetches on four 256-thread CTAs per SM,
+// 70000 columns 2430 against 3154, 32768^2 2348 against 3794 resident on
+// three CTAs per SM: one resident row per SM leaves a bubble at every row
+// boundary that several CTAs per SM hide.
 int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
-  int stages = t.stages ? t.stages : kOnlineDefaultStages;
+  const int64_t widest = std::min<int64_t>(cs::abs_row(g, g.rows - 1) + 1, g.cols);
+  const int64_t widest_vec = (widest + 7) / 8;
+  auto max_stages_for = [&](int64_t tile_bytes) {
+    return (int)std::min<int64_t>(kMaxStages, (d.max_smem_optin - cs::online_tail_bytes(kMaxStages)) / tile_bytes);
+  };
+  const int vpt = t.vec == 1 ? 1 : 2;
+  int stages = t.stages;
   if (!t.stages) {
-    // Rows too long to stay resident in half the default ring are fetched
-    // twice anyway; then a 4-stage ring, which lets 4 CTAs share an SM
-    // instead of 3, is faster (measured on B200 at 65536 and 98304 columns:
-    // 2.69 against 2.39 TB/s).
-    const int64_t widest = std::min<int64_t>(cs::abs_row(g, g.rows - 1) + 1, g.cols);
-    const int64_t tiles = ((widest + 7) / 8 + cs::kOnlineTileVec - 1) / cs::kOnlineTileVec;
-    if (2 * tiles > kOnlineDefaultStages) stages = kOnlineLongRowStages;
+    // Rows that fit the default ring stay resident (one HBM read); longer
+    // rows are fetched twice, on a 4-stage ring, which lets 4 CTAs share an
+    // SM instead of 3 (measured on B200 at 65536 and 98304 columns: 2.69
+    // against 2.39 TB/s; 70000 columns 3213 GB/s against 1662 for a ring
+    // that holds the row on one CTA per SM).
+    const int64_t tile_vec = vpt == 1 ? cs::kOnlineWideThreads : cs::kOnlineTileVec;
+    const int64_t tiles = (widest_vec + tile_vec - 1) / tile_vec;
+    stages = tiles <= kOnlineDefaultStages ? kOnlineDefaultStages : kOnlineLongRowStages;
   }
-  stages = std::max(1, std::min(stages, 24));
-  while (stages > 1 && (int64_t)stages * cs::kOnlineTileBytes + cs::online_tail_bytes(stages) > d.max_smem_optin)
-    --stages;
-  const int smem = stages * cs::kOnlineTileBytes + cs::online_tail_bytes(stages);
+  const int threads = vpt == 1 ? cs::kOnlineWideThreads : cs::kOnlineThreads;
+  const int64_t tile_bytes = (int64_t)threads * vpt * 16;
+  stages = std::max(1, std::min(stages, max_stages_for(tile_bytes)));
+  const int smem = (int)(stages * tile_bytes) + cs::online_tail_bytes(stages);
+  void* fn = vpt == 1 ? reinterpret_cast<void*>(&cs::online_kernel<1>) : reinterpret_cast<void*>(&cs::online_kernel<2>);
   int per_sm = 0;
-  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &per_sm, reinterpret_cast<void*>(&cs::online_kernel), cs::kOnlineThreads, smem));
+  CS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
   if (per_sm < 1) return CS_ERR_UNSUPPORTED;
   const int64_t total_rows = g.batch * g.rows;
   lp->kernel = CS_KERNEL_ONLINE;
   lp->units = total_rows;
   lp->grid = (int)std::min<int64_t>(total_rows, (int64_t)d.sms * per_sm);
-  lp->block = cs::kOnlineThreads;
+  lp->block = threads;
   lp->smem = smem;
   lp->stages = stages;
+  lp->vec = vpt;
   lp->ctas_per_sm = per_sm;
   lp->on.g = g;
   lp->on.total_rows = total_rows;
@@ -604,7 +623,8 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
       break;
     }
     case CS_KERNEL_ONLINE:
-      e = launch_pdl(&cs::online_kernel, lp.grid, lp.block, lp.smem, stream, lp.on);
+      e = lp.vec == 1 ? launch_pdl(&cs::online_kernel<1>, lp.grid, lp.block, lp.smem, stream, lp.on)
+                      : launch_pdl(&cs::online_kernel<2>, lp.grid, lp.block, lp.smem, stream, lp.on);
       break;
     case CS_KERNEL_WARP: {
       void (*k)(cs::NarrowParams) = nullptr;
@@ -630,15 +650,16 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
   return CS_OK;
 }
 
-double modelled_bytes(int kernel, const Geometry& g, int online_stages) {
+// online_ring_vec: 16-byte vectors the online kernel's ring holds (stages x tile).
+double modelled_bytes(int kernel, const Geometry& g, int64_t online_ring_vec) {
   const double t = geometry_causal_elements(g, g.cols);
   const double w = 2.0 * (double)g.rows * (double)g.cols;
   double per = 0;
   switch (kernel) {
     case CS_KERNEL_BASELINE: per = 6.0 * t + w; break;
     case CS_KERNEL_ONLINE: {
-      // Rows longer than half the ring are fetched twice.
-      const int64_t resident_cols = (int64_t)(online_stages / 2) * cs::kOnlineTileVec * 8;
+      // Rows longer than the ring are fetched twice.
+      const int64_t resident_cols = online_ring_vec * 8;
       const double t_long = g.cols > resident_cols
                                 ? std::max(0.0, t - geometry_causal_elements(g, std::min<int64_t>(g.cols, resident_cols)))
                                 : 0.0;
@@ -937,7 +958,7 @@ double cs_logical_bytes(int kernel, int64_t rows, int64_t cols) {
   g.batch = 1;
   g.rows = (int32_t)std::min<int64_t>(rows, kI32Max);
   g.cols = (int32_t)std::min<int64_t>(cols, kI32Max);
-  return modelled_bytes(kernel, g, kOnlineDefaultStages);
+  return modelled_bytes(kernel, g, (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec);
 }
 
 double cs_roofline_bytes(int64_t rows, int64_t cols, int64_t row_offset) {
@@ -1046,10 +1067,10 @@ int cs_plan_set_row_split(cs_plan* plan, int32_t split_row, int32_t split_offset
 int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint, int zero_fill_tma) {
   if (!plan) return CS_ERR_NULL;
   const bool variant_pick = vec_per_thread >= 16 && vec_per_thread < 16 + kNumRowVariants;
-  if (vec_per_thread != 0 && vec_per_thread != 2 && vec_per_thread != 4 && vec_per_thread != 8 &&
-      !variant_pick)
+  if (vec_per_thread != 0 && vec_per_thread != 1 && vec_per_thread != 2 && vec_per_thread != 4 &&
+      vec_per_thread != 8 && !variant_pick)
     return CS_ERR_ARG;
-  if (stages < 0 || stages > 24 || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
+  if (stages < 0 || stages > kMaxStages || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
   if (zero_fill_tma < -1 || zero_fill_tma > 1) return CS_ERR_ARG;
   plan->tuning.vec = vec_per_thread;
   plan->tuning.stages = stages;
@@ -1120,7 +1141,10 @@ int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
   info->algorithmic_bytes =
       (2.0 * geometry_causal_elements(plan->g, plan->g.cols) + 2.0 * (double)plan->g.rows * plan->g.cols) *
       (double)plan->g.batch;
-  info->modelled_bytes = modelled_bytes(lp.kernel, plan->g, lp.stages ? lp.stages : kOnlineDefaultStages);
+  info->modelled_bytes =
+      modelled_bytes(lp.kernel, plan->g,
+                     lp.kernel == CS_KERNEL_ONLINE ? (int64_t)lp.stages * lp.block * lp.vec
+                                                   : (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec);
   return CS_OK;
 }
 

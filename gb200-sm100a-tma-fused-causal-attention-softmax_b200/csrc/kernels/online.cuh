@@ -6,17 +6,20 @@
 // tile in flight per buffer, wait_group(0) after every store):
 //
 //  * each CTA owns whole rows (flat row index blockIdx.x + j*gridDim.x) and a
-//    ring of S shared-memory tiles of 8 KB (512 x 16-byte vectors); thread 0
-//    keeps the ring full with 1-D TMA bulk copies of the causal prefix only,
-//    running ahead across row boundaries;
+//    ring of S shared-memory tiles of VPT 16-byte vectors per thread (256
+//    threads x 2 = 8 KB, or 1024 threads x 1 = 16 KB for long rows, so that a
+//    row of up to ~114K columns stays resident and a whole SM works on it);
+//    thread 0 keeps the ring full with 1-D TMA bulk copies of the causal
+//    prefix only, running ahead across row boundaries;
 //  * pass 1 keeps a per-thread online (max, sum) pair, merged at the end of
 //    the row with warp-shuffle butterflies and one cross-warp exchange;
 //  * pass 2 recomputes exp, scales by the reciprocal of the sum and writes
-//    16-byte vectors straight from registers. When the row occupies at most
-//    half the ring it stays resident in shared memory between the passes, so
-//    HBM sees a single read; longer rows are fetched again for pass 2 (the
-//    first fetch leaves them in L2 with a normal priority, the second marks
-//    them evict-first);
+//    16-byte vectors straight from registers. When the row fits the ring it
+//    stays resident in shared memory between the passes, so HBM sees a single
+//    read, and pass 2 hands each tile back as soon as it is written out, so
+//    the next row's tiles stream in while this row's go out; longer rows are
+//    fetched again for pass 2 (the first fetch leaves them in L2 with a
+//    normal priority, the second marks them evict-first);
 //  * masked columns and padding are 16-byte zero stores.
 //
 // All mbarrier waits are bounded (Geometry::timeout_ns) and report
@@ -28,15 +31,17 @@
 
 namespace cs {
 
-constexpr int kOnlineThreads = 256;
+// Launch shapes: (threads, 16-byte vectors per thread and tile).
+constexpr int kOnlineThreads = 256;  // the default shape: 8 KB tiles
 constexpr int kOnlineVecPerThread = 2;
 constexpr int kOnlineTileVec = kOnlineThreads * kOnlineVecPerThread;  // 512 vectors
 constexpr int kOnlineTileBytes = kOnlineTileVec * 16;                 // 8 KB
+constexpr int kOnlineWideThreads = 1024;  // long rows: 16 KB tiles, one vector per thread
 
 struct OnlineParams {
   Geometry g;
   int64_t total_rows;  // batch * rows
-  int32_t stages;      // ring depth (tiles)
+  int32_t stages;      // ring depth (tiles of blockDim.x * VPT vectors)
 };
 
 __host__ __device__ constexpr int online_tail_bytes(int stages) { return 32 * 8 + stages * 8 + 16; }
@@ -57,14 +62,18 @@ __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float
   m = mn;
 }
 
-__global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_constant__ OnlineParams p) {
+template <int VPT>
+__global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ OnlineParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Geometry& g = p.g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int kWarps = kOnlineThreads / 32;
+  const int nthreads = blockDim.x;
+  const int n_warps = nthreads >> 5;
+  const int32_t tile_vec = nthreads * VPT;             // vectors per tile
+  const size_t tile_bytes = (size_t)tile_vec * 16;
   const int S = p.stages;
   uint8_t* tiles = smem;
-  float2* red = reinterpret_cast<float2*>(smem + (size_t)S * kOnlineTileBytes);
+  float2* red = reinterpret_cast<float2*>(smem + (size_t)S * tile_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + S);
 
@@ -105,22 +114,22 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     int32_t valid;
     row_of(0, p_off, valid);
     p_nvec = (valid + 7) >> 3;
-    p_nt = (p_nvec + kOnlineTileVec - 1) / kOnlineTileVec;
-    p_res = 2 * p_nt <= S;
+    p_nt = (p_nvec + tile_vec - 1) / tile_vec;
+    p_res = p_nt <= S;
     pol_first = policy_evict_first();
   }
   auto produce = [&]() {
     if (skip_loads) return;
     while (loads - released < S && pj < n_rows) {
       const int s = (int)(loads % S);
-      const int32_t v0 = pt * kOnlineTileVec;
-      const int32_t nvt = min(kOnlineTileVec, p_nvec - v0);
+      const int32_t v0 = pt * tile_vec;
+      const int32_t nvt = min(tile_vec, p_nvec - v0);
       mbar_arrive_expect_tx(&full[s], (uint32_t)nvt * 16u);
       const uint16_t* src = g.in + p_off + (int64_t)v0 * 8;
       if (ppass == 0)
-        bulk_g2s(tiles + (size_t)s * kOnlineTileBytes, src, (uint32_t)nvt * 16u, &full[s]);
+        bulk_g2s(tiles + (size_t)s * tile_bytes, src, (uint32_t)nvt * 16u, &full[s]);
       else
-        bulk_g2s_hint(tiles + (size_t)s * kOnlineTileBytes, src, (uint32_t)nvt * 16u, &full[s], pol_first);
+        bulk_g2s_hint(tiles + (size_t)s * tile_bytes, src, (uint32_t)nvt * 16u, &full[s], pol_first);
       ++loads;
       if (++pt == p_nt) {
         pt = 0;
@@ -132,8 +141,8 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
             int32_t valid;
             row_of(pj, p_off, valid);
             p_nvec = (valid + 7) >> 3;
-            p_nt = (p_nvec + kOnlineTileVec - 1) / kOnlineTileVec;
-            p_res = 2 * p_nt <= S;
+            p_nt = (p_nvec + tile_vec - 1) / tile_vec;
+            p_res = p_nt <= S;
           }
         }
       }
@@ -148,8 +157,8 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     int32_t valid;
     row_of(j, off, valid);
     const int32_t nvec = (valid + 7) >> 3;
-    const int32_t nt = (nvec + kOnlineTileVec - 1) / kOnlineTileVec;
-    const bool resident = 2 * nt <= S;
+    const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
+    const bool resident = nt <= S;
 
     // Pass 1: online (max, sum) over this thread's vectors.
     float m = -INFINITY, s = 0.f;
@@ -163,11 +172,11 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
         *abort_flag = 1;
       } else {
 #pragma unroll
-        for (int q = 0; q < kOnlineVecPerThread; ++q) {
-          const int32_t lv = tid + q * kOnlineThreads;  // vector within the tile
-          const int32_t v = t * kOnlineTileVec + lv;    // vector within the row
+        for (int q = 0; q < VPT; ++q) {
+          const int32_t lv = tid + q * nthreads;  // vector within the tile
+          const int32_t v = t * tile_vec + lv;    // vector within the row
           if (v < nvec) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * kOnlineTileBytes + (size_t)lv * 16);
+            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * tile_bytes + (size_t)lv * 16);
             const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
             const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
             const float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
@@ -203,7 +212,7 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
     if (lane == 0) red[warp] = make_float2(m, s);
     __syncthreads();
     if (*abort_flag) { aborted = true; break; }
-    float2 w = lane < kWarps ? red[lane] : make_float2(-INFINITY, 0.f);
+    float2 w = lane < n_warps ? red[lane] : make_float2(-INFINITY, 0.f);
     float rm = w.x, rs = w.y;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -229,11 +238,11 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
       }
       if (ok) {
 #pragma unroll
-        for (int q = 0; q < kOnlineVecPerThread; ++q) {
-          const int32_t lv = tid + q * kOnlineThreads;
-          const int32_t v = t * kOnlineTileVec + lv;
+        for (int q = 0; q < VPT; ++q) {
+          const int32_t lv = tid + q * nthreads;
+          const int32_t v = t * tile_vec + lv;
           if (v < nvec) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * kOnlineTileBytes + (size_t)lv * 16);
+            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * tile_bytes + (size_t)lv * 16);
             const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
             const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
             float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
@@ -249,20 +258,16 @@ __global__ void __launch_bounds__(kOnlineThreads) online_kernel(const __grid_con
           }
         }
       }
-      if (!resident) {
-        __syncthreads();
-        if (*abort_flag) { aborted = true; break; }
-        if (tid == 0) { released = idx + 1; produce(); }
-      }
+      // The tile is written out: hand its stage back (this row's next tiles
+      // are already in their stages; the stage fills with a later tile).
+      __syncthreads();
+      if (*abort_flag) { aborted = true; break; }
+      if (tid == 0) { released = idx + 1; produce(); }
     }
     if (aborted) break;
-    if (resident) {
-      __syncthreads();  // every thread is done with this row's tiles
-      if (tid == 0) { released = base + nt; produce(); }
-    }
     base += resident ? nt : 2 * nt;
 
-    for (int32_t v = nvec + tid; v < pv; v += kOnlineThreads)
+    for (int32_t v = nvec + tid; v < pv; v += nthreads)
       *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = make_uint4(0u, 0u, 0u, 0u);
   }
 

@@ -191,8 +191,10 @@ int cs_plan_set_row_split(cs_plan *plan, int32_t split_row, int32_t split_offset
 
 /* Tuning knobs (0 / -1 = automatic): vectors per thread of the TMA /
  * PIPELINE kernels (2, 4 or 8; 16 + i selects compiled variant i of the
- * row-resident kernel directly), ring stages of the TMA / PIPELINE / ONLINE
- * kernels (1..24), L2 evict-first hint on the input copies (0 off, 1 on),
+ * row-resident kernel directly) or of the ONLINE kernel (2: 256-thread CTAs
+ * with 8 KB tiles, 1: 1024-thread CTAs with 16 KB tiles), ring stages of the TMA / PIPELINE / ONLINE
+ * kernels (1..32; fewer where shared memory does not hold them), L2
+ * evict-first hint on the input copies (0 off, 1 on),
  * masked columns written by TMA bulk stores (1) or by thread stores (0). */
 int cs_plan_set_tuning(cs_plan *plan, int vec_per_thread, int stages, int l2_hint,
                        int zero_fill_tma);

@@ -486,8 +486,27 @@ def test_unpaired_fallback_when_a_pair_does_not_fit():
             check(from_dev(d_out), x, cols=cols, scale=0.0883883, row_offset=off, what=kernel)
 
 
+def test_online_very_long_rows():
+    # Rows far beyond the row-resident kernel (which holds a pair of up to
+    # ~56K columns): one 100000-column row, and 64 rows of ~70000 columns in
+    # a batch of two, with the automatic ring (the whole row resident in
+    # shared memory) and with rings too short for it (two fetches per row).
+    for rows, cols, off, batch in [(1, 100000, 99999, 1), (64, 70000, 69936, 2)]:
+        x = cs.generate(5, 4, batch=batch, rows=rows, cols=cols, first_row=off)
+        # Automatic; 8 KB tiles, two fetches or the row resident; the
+        # 1024-thread shape with 16 KB tiles, resident and two fetches.
+        for tuning in (None, (0, 4, -1, -1), (0, 27, -1, -1), (1, 13, -1, -1), (1, 4, -1, -1)):
+            got = run("online", x if batch > 1 else x[0], cols=cols, scale=0.0883883, row_offset=off,
+                      tuning=tuning)
+            g = got.reshape(batch, rows, -1)
+            for b in range(batch):
+                check(g[b], x[b], cols=cols, scale=0.0883883, row_offset=off,
+                      what=f"online {batch}x{rows}x{cols}+{off} tuning {tuning}")
+        assert cs.resolve_kernel("auto", off + rows, cols) == "online" or cols <= 56000
+
+
 def test_online_ring_depths_and_long_rows():
-    # Rows longer than half the ring take the two-fetch path.
+    # Rows longer than the ring take the two-fetch path.
     for stages in (2, 3, 8, 16):
         for rows, cols in [(40, 20000), (3, 70000), (600, 4100)]:
             x = cs.generate(5, 4, batch=1, rows=rows, cols=cols)[0]
