@@ -38,6 +38,7 @@ BUDGETS = [
      "V = 8 at up to 14 warps; only a tuning request selects it since the shared-memory "
      "variant (V = 0) serves long rows"),
     (r"online_kernel<[12]>", 64, 0, "launch bounds of 1024 threads (the long-row shape)"),
+    (r"cluster_kernel", 64, 0, "shared-memory passes with 17 warps per CTA; nothing to keep in registers"),
     (r"rowres_kernel<8, 256, 1, [01]>", 168, 0, "V = 8 at up to 8 warps; tuning request only"),
     (r"rowres_kernel<0, 1024, 1, [01]>", 64, 0, "shared-memory passes, 32 warps in one CTA"),
 ]

@@ -21,6 +21,7 @@
 
 #include "causal_softmax.h"
 #include "kernels/baseline.cuh"
+#include "kernels/cluster.cuh"
 #include "kernels/narrow.cuh"
 #include "kernels/online.cuh"
 #include "kernels/rowres.cuh"
@@ -157,6 +158,8 @@ int device_info(int dev, DeviceInfo** out) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::online_kernel<2>),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::cluster_kernel),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     // Every other kernel a launch may pick, so that the driver has all of the
     // library's code in place once this set-up is done (it may take device
     // memory for it); later launches then add nothing on the device.
@@ -240,6 +243,8 @@ struct LaunchPlan {
   int narrow_lanes = 0;
   cs::RowResParams rr{};
   cs::OnlineParams on{};
+  bool cluster = false;    // online: the cluster-resident kernel (cl) instead of on
+  cs::ClusterParams cl{};
   cs::NarrowParams nr{};
   cs::BaselineParams bl{};
 };
@@ -442,7 +447,67 @@ int plan_rowres(const DeviceInfo& d, const Geometry& g, const Tuning& t, bool tm
 // 70000 columns 2430 against 3154, 32768^2 2348 against 3794 resident on
 // three CTAs per SM: one resident row per SM leaves a bubble at every row
 // boundary that several CTAs per SM hide.
+// Cluster-resident online kernel: a row's blocks of 2 KB are dealt over the
+// C CTAs of a cluster, so each CTA holds stage_blocks blocks of a row per
+// stage. C is the smallest of 2, 4, 8 that keeps a stage within 24 blocks
+// (48 KB), so that two stages of a few CTAs fit an SM; rows needing more are
+// not served (CS_ERR_UNSUPPORTED).
+int plan_cluster(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+  const int64_t pv = g.pitch / 8;
+  const int64_t nblk = (pv + cs::kClusterBlockVec - 1) / cs::kClusterBlockVec;
+  int csize = 0;
+  int64_t stage_blocks = 0;
+  for (int c : {2, 4, 8}) {
+    stage_blocks = (nblk + c - 1) / c;
+    if (stage_blocks <= 24) {
+      csize = c;
+      break;
+    }
+  }
+  if (!csize) {
+    std::snprintf(t_detail, sizeof t_detail, "cluster kernel: rows of %lld vectors exceed 8 CTAs x 24 blocks",
+                  (long long)pv);
+    return CS_ERR_UNSUPPORTED;
+  }
+  const int stages = t.stages ? std::max(2, std::min(t.stages, 8)) : 2;
+  const int warps = (int)std::max<int64_t>(2, std::min<int64_t>(16, stage_blocks));
+  const int block = 32 * (warps + 1);
+  const int smem = (int)(stages * stage_blocks * cs::kClusterBlockVec * 16) + cs::cluster_tail_bytes(stages);
+  if (smem > d.max_smem_optin) return CS_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(csize * d.sms));
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  CS_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, reinterpret_cast<void*>(&cs::cluster_kernel), &cfg));
+  if (max_clusters < 1) return CS_ERR_UNSUPPORTED;
+  const int64_t total_rows = g.batch * g.rows;
+  lp->kernel = CS_KERNEL_ONLINE;
+  lp->cluster = true;
+  lp->units = total_rows;
+  lp->grid = (int)(std::min<int64_t>(total_rows, max_clusters) * csize);
+  lp->block = block;
+  lp->smem = smem;
+  lp->stages = stages;
+  lp->vec = 3;
+  lp->ctas_per_sm = (int)std::max<int64_t>(1, (int64_t)max_clusters * csize / d.sms);
+  lp->cl.g = g;
+  lp->cl.total_rows = total_rows;
+  lp->cl.csize = csize;
+  lp->cl.stage_blocks = (int32_t)stage_blocks;
+  lp->cl.stages = stages;
+  return CS_OK;
+}
+
 int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchPlan* lp) {
+  if (t.vec == 3) return plan_cluster(d, g, t, lp);
   const int64_t widest = std::min<int64_t>(cs::abs_row(g, g.rows - 1) + 1, g.cols);
   const int64_t widest_vec = (widest + 7) / 8;
   auto max_stages_for = [&](int64_t tile_bytes) {
@@ -570,6 +635,7 @@ int make_plan(const DeviceInfo& d, int kernel, const Geometry& g, const Tuning& 
       lp->rr.g = g;  // pointers, scale, status word, flags and timeout of this call
       if (!lp->dyn_sched) lp->rr.g.sched = nullptr;
       lp->on.g = g;
+      lp->cl.g = g;
       lp->nr.g = g;
       lp->bl.g = g;
       return CS_OK;
@@ -623,6 +689,24 @@ int launch_plan(const LaunchPlan& lp, cudaStream_t stream) {
       break;
     }
     case CS_KERNEL_ONLINE:
+      if (lp.cluster) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)lp.grid);
+        cfg.blockDim = dim3((unsigned)lp.block);
+        cfg.dynamicSmemBytes = (size_t)lp.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)lp.cl.csize;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        e = cudaLaunchKernelEx(&cfg, &cs::cluster_kernel, lp.cl);
+        break;
+      }
       e = lp.vec == 1 ? launch_pdl(&cs::online_kernel<1>, lp.grid, lp.block, lp.smem, stream, lp.on)
                       : launch_pdl(&cs::online_kernel<2>, lp.grid, lp.block, lp.smem, stream, lp.on);
       break;
@@ -1067,8 +1151,8 @@ int cs_plan_set_row_split(cs_plan* plan, int32_t split_row, int32_t split_offset
 int cs_plan_set_tuning(cs_plan* plan, int vec_per_thread, int stages, int l2_hint, int zero_fill_tma) {
   if (!plan) return CS_ERR_NULL;
   const bool variant_pick = vec_per_thread >= 16 && vec_per_thread < 16 + kNumRowVariants;
-  if (vec_per_thread != 0 && vec_per_thread != 1 && vec_per_thread != 2 && vec_per_thread != 4 &&
-      vec_per_thread != 8 && !variant_pick)
+  if (vec_per_thread != 0 && vec_per_thread != 1 && vec_per_thread != 2 && vec_per_thread != 3 &&
+      vec_per_thread != 4 && vec_per_thread != 8 && !variant_pick)
     return CS_ERR_ARG;
   if (stages < 0 || stages > kMaxStages || l2_hint < -1 || l2_hint > 1) return CS_ERR_ARG;
   if (zero_fill_tma < -1 || zero_fill_tma > 1) return CS_ERR_ARG;
@@ -1143,8 +1227,9 @@ int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
       (double)plan->g.batch;
   info->modelled_bytes =
       modelled_bytes(lp.kernel, plan->g,
-                     lp.kernel == CS_KERNEL_ONLINE ? (int64_t)lp.stages * lp.block * lp.vec
-                                                   : (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec);
+                     lp.cluster ? (int64_t)plan->g.pitch  // the whole row resident in the cluster
+                     : lp.kernel == CS_KERNEL_ONLINE ? (int64_t)lp.stages * lp.block * lp.vec
+                                                     : (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec);
   return CS_OK;
 }
 

@@ -505,6 +505,34 @@ def test_online_very_long_rows():
         assert cs.resolve_kernel("auto", off + rows, cols) == "online" or cols <= 56000
 
 
+@pytest.mark.parametrize("stages", [0, 3])
+def test_cluster_resident_online_kernel(stages):
+    # Tuning vec 3 runs `online` on the cluster kernel: each row dealt in 2 KB
+    # blocks over the 2, 4 or 8 CTAs of a thread-block cluster, the partial
+    # (max, sum) exchanged through distributed shared memory. Cluster sizes
+    # 2/4/8 (row widths of up to 48, 96 and 192 blocks), odd pitch, batches,
+    # row offsets, zero scale, rows shorter than one block of some CTAs.
+    cases = [(300, 4096, 0, 1, 0.0883883), (64, 12000, 20000, 2, 1.0), (1000, 1037, 0, 1, 0.0883883),
+             (33, 100000, 99967, 1, 0.0883883), (700, 700, 0, 3, 0.5), (40, 20000, 0, 1, 0.0),
+             (16, 70000, 69984, 2, 0.125)]
+    for rows, cols, off, batch, scale in cases:
+        x = cs.generate(5, 4, batch=batch, rows=rows, cols=cols, first_row=off)
+        got = run("online", x if batch > 1 else x[0], cols=cols, scale=scale, row_offset=off,
+                  tuning=(3, stages, -1, -1))
+        g = got.reshape(batch, rows, -1)
+        for b in range(batch):
+            check(g[b], x[b], cols=cols, scale=scale, row_offset=off,
+                  what=f"cluster online {batch}x{rows}x{cols}+{off} scale {scale} S={stages}")
+    # The launch is a cluster launch of the online kernel.
+    d_in = to_dev(cs.generate(5, 4, batch=1, rows=8, cols=100000, first_row=99992)[0])
+    d_out = sentinel_like(d_in)
+    with cs.Plan.for_tensors(d_in, d_out, cols=100000, row_offset=99992) as plan:
+        plan.set_tuning(3, stages, -1, -1)
+        info = plan.describe("online")
+        assert info["kernel_name"] == "online" and info["vec_per_thread"] == 3
+        assert info["grid"] % 8 == 0  # 98 blocks per row: clusters of 8
+
+
 def test_online_ring_depths_and_long_rows():
     # Rows longer than the ring take the two-fetch path.
     for stages in (2, 3, 8, 16):
@@ -592,7 +620,8 @@ def test_session_paths():
 
 
 @pytest.mark.parametrize("kernel,tuning", [("tma", None), ("pipeline", None), ("online", None),
-                                           ("tma", (23, 0, -1, -1)), ("pipeline", (23, 0, -1, -1))])
+                                           ("tma", (23, 0, -1, -1)), ("pipeline", (23, 0, -1, -1)),
+                                           ("online", (3, 0, -1, -1))])
 def test_bounded_wait_reports_timeout_and_context_survives(kernel, tuning):
     # The producer issues no copies, so every consumer wait must run out after
     # 1 ms; the kernel returns, the host reads CS_ERR_TIMEOUT, and the next

@@ -20,7 +20,7 @@ def test_library_report_passes_the_gate():
     # Every launchable kernel family is reported: 8 row-resident variants x 2
     # store modes, the two online shapes, baseline and 6 narrow instantiations.
     assert sum(n.startswith("rowres_kernel<") for n in names) == 16
-    assert {"online_kernel<1>", "online_kernel<2>", "baseline_kernel", "probe_kernel"} <= names
+    assert {"online_kernel<1>", "online_kernel<2>", "baseline_kernel", "probe_kernel", "cluster_kernel"} <= names
     assert sum(n.startswith("narrow_kernel<") for n in names) == 6
 
 
