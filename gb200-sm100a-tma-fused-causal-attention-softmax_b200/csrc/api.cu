@@ -160,6 +160,8 @@ int device_info(int dev, DeviceInfo** out) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
     CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::cluster_kernel),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin));
+    CS_CUDA(cudaFuncSetAttribute(reinterpret_cast<void*>(&cs::cluster_kernel),
+                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     // Every other kernel a launch may pick, so that the driver has all of the
     // library's code in place once this set-up is done (it may take device
     // memory for it); later launches then add nothing on the device.
@@ -457,7 +459,7 @@ int plan_cluster(const DeviceInfo& d, const Geometry& g, const Tuning& t, Launch
   const int64_t nblk = (pv + cs::kClusterBlockVec - 1) / cs::kClusterBlockVec;
   int csize = 0;
   int64_t stage_blocks = 0;
-  for (int c : {2, 4, 8}) {
+  for (int c : {2, 4, 8, 16}) {
     stage_blocks = (nblk + c - 1) / c;
     if (stage_blocks <= 24) {
       csize = c;
@@ -465,7 +467,7 @@ int plan_cluster(const DeviceInfo& d, const Geometry& g, const Tuning& t, Launch
     }
   }
   if (!csize) {
-    std::snprintf(t_detail, sizeof t_detail, "cluster kernel: rows of %lld vectors exceed 8 CTAs x 24 blocks",
+    std::snprintf(t_detail, sizeof t_detail, "cluster kernel: rows of %lld vectors exceed 16 CTAs x 24 blocks",
                   (long long)pv);
     return CS_ERR_UNSUPPORTED;
   }
@@ -514,19 +516,23 @@ int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchP
     return (int)std::min<int64_t>(kMaxStages, (d.max_smem_optin - cs::online_tail_bytes(kMaxStages)) / tile_bytes);
   };
   const int vpt = t.vec == 1 ? 1 : 2;
+  // Automatic shape: rows of at most two default tiles take the short shape
+  // (measured on B200 at 64 x 4096^2: 3182 GB/s with six CTAs per SM against
+  // 2307 for the default shape's three); longer rows the default shape,
+  // which leads at 32768, 70000 and 100000 columns.
+  const bool short_rows = t.vec == 0 && widest_vec <= 2 * (int64_t)cs::kOnlineTileVec;
+  const int threads = vpt == 1 ? cs::kOnlineWideThreads : short_rows ? cs::kOnlineShortThreads : cs::kOnlineThreads;
+  const int64_t tile_vec = cs::online_tile_vec(threads, vpt);
   int stages = t.stages;
   if (!t.stages) {
     // Rows that fit the default ring stay resident (one HBM read); longer
     // rows are fetched twice, on a 4-stage ring, which lets 4 CTAs share an
-    // SM instead of 3 (measured on B200 at 65536 and 98304 columns: 2.69
-    // against 2.39 TB/s; 70000 columns 3213 GB/s against 1662 for a ring
-    // that holds the row on one CTA per SM).
-    const int64_t tile_vec = vpt == 1 ? cs::kOnlineWideThreads : cs::kOnlineTileVec;
+    // SM instead of 3 (measured on B200 at 2048 x 100000 columns: 3824
+    // against 3276 GB/s for 8 stages; 5 and 6 stages tie with 4).
     const int64_t tiles = (widest_vec + tile_vec - 1) / tile_vec;
     stages = tiles <= kOnlineDefaultStages ? kOnlineDefaultStages : kOnlineLongRowStages;
   }
-  const int threads = vpt == 1 ? cs::kOnlineWideThreads : cs::kOnlineThreads;
-  const int64_t tile_bytes = (int64_t)threads * vpt * 16;
+  const int64_t tile_bytes = tile_vec * 16;
   stages = std::max(1, std::min(stages, max_stages_for(tile_bytes)));
   const int smem = (int)(stages * tile_bytes) + cs::online_tail_bytes(stages);
   void* fn = vpt == 1 ? reinterpret_cast<void*>(&cs::online_kernel<1>) : reinterpret_cast<void*>(&cs::online_kernel<2>);
@@ -1228,7 +1234,7 @@ int cs_plan_describe(cs_plan* plan, int kernel, cs_launch_info* info) {
   info->modelled_bytes =
       modelled_bytes(lp.kernel, plan->g,
                      lp.cluster ? (int64_t)plan->g.pitch  // the whole row resident in the cluster
-                     : lp.kernel == CS_KERNEL_ONLINE ? (int64_t)lp.stages * lp.block * lp.vec
+                     : lp.kernel == CS_KERNEL_ONLINE ? (int64_t)lp.stages * cs::online_tile_vec(lp.block, lp.vec)
                                                      : (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec);
   return CS_OK;
 }

@@ -38,7 +38,7 @@
 
 namespace cs {
 
-constexpr int kClusterMax = 8;         // CTAs per cluster (portable limit)
+constexpr int kClusterMax = 16;        // CTAs per cluster (above 8: the non-portable opt-in)
 constexpr int kClusterBlockVec = 128;  // vectors per block (2 KB)
 constexpr int kClusterZeroBytes = kClusterBlockVec * 16;
 
@@ -100,21 +100,6 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_
     if (mbar_try_wait_parity_cluster(bar, parity, 200000u)) return true;
     if (global_timer_ns() - start > timeout_ns) return false;
   }
-}
-
-// Barrier among the first `nthreads` threads (named barrier `id`) that also
-// ORs a predicate over them: every participant gets the same answer.
-__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
-      : "memory");
-  return r != 0;
 }
 
 __device__ __forceinline__ void cluster_sync_all() {

@@ -168,6 +168,21 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Barrier among the first `nthreads` threads (named barrier `id`) that also
+// ORs a predicate over them: every participant gets the same answer.
+__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // MUFU base-2 exponential (PTX ex2.approx; subnormal results flush to zero,
 // which cannot change an FP16 probability: p <= e and e < 2^-126 rounds to 0).
 __device__ __forceinline__ float ex2(float x) {

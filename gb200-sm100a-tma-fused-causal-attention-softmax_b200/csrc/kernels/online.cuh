@@ -1,18 +1,24 @@
 // Pipelined online-softmax causal kernel for long rows (the `online` kernel
-// choice, and the automatic choice once a row no longer fits the
-// row-resident kernel's registers).
+// choice, and the automatic choice once a row pair no longer fits two stages
+// of the row-resident kernel).
 //
 // Replaces gpu/src/main.rs:546-727 (two dense TMA passes, 2 KB tiles, one
 // tile in flight per buffer, wait_group(0) after every store):
 //
 //  * each CTA owns whole rows (flat row index blockIdx.x + j*gridDim.x) and a
-//    ring of S shared-memory tiles of VPT 16-byte vectors per thread (256
-//    threads x 2 = 8 KB, or 1024 threads x 1 = 16 KB for long rows, so that a
-//    row of up to ~114K columns stays resident and a whole SM works on it);
-//    thread 0 keeps the ring full with 1-D TMA bulk copies of the causal
-//    prefix only, running ahead across row boundaries;
-//  * pass 1 keeps a per-thread online (max, sum) pair, merged at the end of
-//    the row with warp-shuffle butterflies and one cross-warp exchange;
+//    ring of S shared-memory tiles; a tile is W consumer warps x 32 lanes x
+//    VPT 16-byte vectors (8 warps x 2 = 8 KB by default, 31 warps x 1 =
+//    15.5 KB for the wide shape);
+//  * one producer warp keeps the ring full with 1-D TMA bulk copies of the
+//    causal prefix only, running ahead across row boundaries, and writes the
+//    masked columns and pitch padding with bulk stores from a zero buffer;
+//    it refills a stage once all W consumer warps have arrived on the
+//    stage's `empty` mbarrier, so no CTA-wide barrier runs per tile;
+//  * pass 1 keeps a per-lane online (max, sum) pair: the max of a vector is
+//    taken on packed halves, the sum is rescaled only when that max grows,
+//    and the exponents (x - m) * sl run on packed f32 pairs (x == m gives
+//    exactly 0 at any scale, up to 1e30); the row's pairs are merged with a
+//    redux max and a rescaled warp sum, and one consumer-only barrier per row;
 //  * pass 2 recomputes exp, scales by the reciprocal of the sum and writes
 //    16-byte vectors straight from registers. When the row fits the ring it
 //    stays resident in shared memory between the passes, so HBM sees a single
@@ -20,10 +26,13 @@
 //    the next row's tiles stream in while this row's go out; longer rows are
 //    fetched again for pass 2 (the first fetch leaves them in L2 with a
 //    normal priority, the second marks them evict-first);
-//  * masked columns and padding are 16-byte zero stores.
+//  * a zero scale (every causal probability 1/valid) is a separate
+//    instantiation of the consumer passes, so no per-element test of it runs.
 //
 // All mbarrier waits are bounded (Geometry::timeout_ns) and report
-// kStatusTimeout through the status word.
+// kStatusTimeout through the status word; the consumers leave a row together
+// (a barrier that ORs their verdicts), and the producer stops at the abort
+// flag and waits, bounded, for its copies in flight before it returns.
 #pragma once
 
 #include "common.cuh"
@@ -31,35 +40,198 @@
 
 namespace cs {
 
-// Launch shapes: (threads, 16-byte vectors per thread and tile).
-constexpr int kOnlineThreads = 256;  // the default shape: 8 KB tiles
+// Launch shapes: consumer warps and 16-byte vectors per lane and tile; one
+// more warp is the producer.
+constexpr int kOnlineConsumerWarps = 8;  // the default shape: 8 KB tiles
 constexpr int kOnlineVecPerThread = 2;
-constexpr int kOnlineTileVec = kOnlineThreads * kOnlineVecPerThread;  // 512 vectors
-constexpr int kOnlineTileBytes = kOnlineTileVec * 16;                 // 8 KB
-constexpr int kOnlineWideThreads = 1024;  // long rows: 16 KB tiles, one vector per thread
+constexpr int kOnlineThreads = 32 * (kOnlineConsumerWarps + 1);
+constexpr int kOnlineTileVec = 32 * kOnlineConsumerWarps * kOnlineVecPerThread;  // 512 vectors
+constexpr int kOnlineTileBytes = kOnlineTileVec * 16;                             // 8 KB
+constexpr int kOnlineWideThreads = 1024;  // long rows: 31 consumer warps, one vector per lane
+// Rows of at most two default tiles: 4 consumer warps (4 KB tiles), so that
+// six CTAs, each with a ring of 8 stages, share an SM.
+constexpr int kOnlineShortConsumerWarps = 4;
+constexpr int kOnlineShortThreads = 32 * (kOnlineShortConsumerWarps + 1);
+constexpr int kOnlineZeroBytes = 4096;    // zero buffer for the masked columns' bulk stores
+
+// Vectors of one tile for a CTA of `threads` threads and VPT vectors per lane.
+__host__ __device__ constexpr int online_tile_vec(int threads, int vpt) { return (threads - 32) * vpt; }
 
 struct OnlineParams {
   Geometry g;
   int64_t total_rows;  // batch * rows
-  int32_t stages;      // ring depth (tiles of blockDim.x * VPT vectors)
+  int32_t stages;      // ring depth (tiles)
 };
 
-__host__ __device__ constexpr int online_tail_bytes(int stages) { return 32 * 8 + stages * 8 + 16; }
+// Shared memory after the tiles: zero buffer, two rows' warp partials,
+// full and empty mbarriers per stage, the abort flag.
+__host__ __device__ constexpr int online_tail_bytes(int stages) {
+  return kOnlineZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
+}
 
-// (m, s) merge of two online-softmax partial states.
-// m are row maxima of the raw values; sl = scale*log2(e).
-// An empty state has m == -inf; it is handled apart because (-inf - mn) * sl
-// is NaN when the scale is 0.
-__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2, float sl) {
-  if (m2 == -INFINITY) return;
-  if (m == -INFINITY) {
-    m = m2;
-    s = s2;
-    return;
+// Flat row j of this CTA -> element offset of its first column and its
+// number of causal (valid) columns.
+__device__ __forceinline__ void online_row(const Geometry& g, int64_t j, int64_t& off, int32_t& valid) {
+  const int64_t flat = (int64_t)blockIdx.x + j * (int64_t)gridDim.x;
+  const int64_t b = flat / g.rows;
+  const int32_t i = (int32_t)(flat - b * g.rows);
+  off = b * g.batch_stride + (int64_t)i * g.pitch;
+  valid = valid_cols(g, i);
+}
+
+// The W consumer warps: both passes over every row of the CTA. A lane takes
+// vectors warp*32 + lane + q*32W (q < VPT) of each tile, so each warp reads
+// 512 contiguous bytes per load.
+template <int VPT, bool kZeroScale>
+__device__ __forceinline__ void online_consumers(const OnlineParams& p, const uint8_t* tiles, float2* red,
+                                                 uint64_t* full, uint64_t* empty, volatile int* abort_flag,
+                                                 int64_t n_rows, int warp, int lane, int W) {
+  const Geometry& g = p.g;
+  const int S = p.stages;
+  const int32_t tile_vec = 32 * W * VPT;
+  const size_t tile_bytes = (size_t)tile_vec * 16;
+  const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
+  const float2 sl2 = make_float2(sl, sl);
+  const int32_t lv0 = warp * 32 + lane;
+  int64_t idx = 0;  // load index of the current row's first tile
+  for (int64_t j = 0; j < n_rows; ++j) {
+    int64_t off;
+    int32_t valid;
+    online_row(g, j, off, valid);
+    const int32_t nvec = (valid + 7) >> 3;
+    const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
+    const bool resident = nt <= S;
+    // Vector v of the row, from lane slot lv of stage st; halves past the
+    // causal boundary read as -inf (they lose the max and give exp 0).
+    auto vec_at = [&](int st, int32_t v, int32_t lv) {
+      uint4 r = *reinterpret_cast<const uint4*>(tiles + (size_t)st * tile_bytes + (size_t)lv * 16);
+      const int32_t lim = valid - v * 8;
+      if (lim < 8) r = mask_tail_neg_inf(r, lim);
+      return r;
+    };
+
+    // Pass 1: this lane's online (max, sum); zero scale: its count of
+    // elements that are not -inf.
+    float m = -INFINITY;
+    float2 acc = make_float2(0.f, 0.f);
+    bool bad = false;  // a wait ran out: skip the rest of the row's waits
+    for (int32_t t = 0; t < nt; ++t) {
+      const int64_t li = idx + t;
+      const int st = (int)(li % S);
+      if (!bad && !mbar_wait_bounded(&full[st], (uint32_t)((li / S) & 1), g.timeout_ns)) {
+        bad = true;
+        *abort_flag = 1;
+        if (g.status) atomicOr(g.status, kStatusTimeout);
+      }
+      if (!bad) {
+#pragma unroll
+        for (int q = 0; q < VPT; ++q) {
+          const int32_t lv = q * 32 * W + lv0;
+          const int32_t v = t * tile_vec + lv;
+          if (v < nvec) {
+            const uint4 r = vec_at(st, v, lv);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+            if constexpr (kZeroScale) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                acc.x += (w4[e] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
+                acc.y += (w4[e] >> 16) == kHalfNegInf ? 0.f : 1.f;
+              }
+            } else {
+              const float vm = __half2float(max8_half(r));
+              if (vm > m) {
+                // (m - vm) * sl is -inf while m is -inf: the empty sum stays 0.
+                const float c = ex2((m - vm) * sl);
+                acc = __fmul2_rn(acc, make_float2(c, c));
+                m = vm;
+              }
+              if (m > -INFINITY) {
+                const float2 nm2 = make_float2(-m, -m);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[e])), nm2), sl2);
+                  acc = __fadd2_rn(acc, make_float2(ex2(d.x), ex2(d.y)));
+                }
+              }
+            }
+          }
+        }
+      }
+      if (!resident) {
+        // Fetched again for pass 2: this warp is done with the stage.
+        __syncwarp();
+        if (lane == 0 && !bad) mbar_arrive(&empty[st]);
+      }
+    }
+
+    // Row statistics: the warp's max (one redux instruction) and the sum of
+    // its lanes' sums rescaled to it, then the same across the consumer warps.
+    float s = acc.x + acc.y;
+    if constexpr (!kZeroScale) {
+      const float wm = redux_max(m);
+      s = m > -INFINITY ? s * ex2((m - wm) * sl) : 0.f;
+      m = wm;
+    }
+    s = warp_sum(s);
+    float2* rk = red + (j & 1) * 32;  // two rows' slots: a warp runs at most one row ahead
+    if (lane == 0) rk[warp] = make_float2(m, s);
+    if (bar_red_or(1, W * 32, bad || *abort_flag != 0)) {
+      *abort_flag = 1;
+      break;
+    }
+    const float2 w = lane < W ? rk[lane] : make_float2(-INFINITY, 0.f);
+    float rm = -INFINITY, rs;
+    if constexpr (kZeroScale) {
+      rs = warp_sum(w.y);
+    } else {
+      rm = redux_max(w.x);
+      rs = warp_sum(w.x > -INFINITY ? w.y * ex2((w.x - rm) * sl) : 0.f);
+    }
+    const float inv = rcp_rn(rs);
+    const float2 inv2 = make_float2(inv, inv);
+    const float2 nM2 = make_float2(-rm, -rm);
+
+    // Pass 2: normalise and write; each tile's stage is handed back after it.
+    uint16_t* out_row = g.out + off;
+    for (int32_t t = 0; t < nt; ++t) {
+      const int64_t li = resident ? idx + t : idx + nt + t;
+      const int st = (int)(li % S);
+      if (!resident && !bad && !mbar_wait_bounded(&full[st], (uint32_t)((li / S) & 1), g.timeout_ns)) {
+        bad = true;
+        *abort_flag = 1;
+        if (g.status) atomicOr(g.status, kStatusTimeout);
+      }
+      if (!bad) {
+#pragma unroll
+        for (int q = 0; q < VPT; ++q) {
+          const int32_t lv = q * 32 * W + lv0;
+          const int32_t v = t * tile_vec + lv;
+          if (v < nvec) {
+            const uint4 r = vec_at(st, v, lv);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 x;
+              if constexpr (kZeroScale) {
+                x.x = (w4[e] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
+                x.y = (w4[e] >> 16) == kHalfNegInf ? 0.f : 1.f;
+              } else {
+                const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[e])), nM2), sl2);
+                x = make_float2(ex2(d.x), ex2(d.y));
+              }
+              const float2 pr = __fmul2_rn(x, inv2);
+              o[e] = float2_to_half2_bits(pr.x, pr.y);
+            }
+            *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && !bad) mbar_arrive(&empty[st]);
+    }
+    idx += resident ? nt : 2 * nt;
   }
-  const float mn = fmaxf(m, m2);
-  s = s * ex2((m - mn) * sl) + s2 * ex2((m2 - mn) * sl);
-  m = mn;
 }
 
 template <int VPT>
@@ -67,215 +239,108 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
   extern __shared__ __align__(128) uint8_t smem[];
   const Geometry& g = p.g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nthreads = blockDim.x;
-  const int n_warps = nthreads >> 5;
-  const int32_t tile_vec = nthreads * VPT;             // vectors per tile
+  const int W = (blockDim.x >> 5) - 1;  // consumer warps; warp W is the producer
+  const int32_t tile_vec = 32 * W * VPT;
   const size_t tile_bytes = (size_t)tile_vec * 16;
   const int S = p.stages;
   uint8_t* tiles = smem;
-  float2* red = reinterpret_cast<float2*>(smem + (size_t)S * tile_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 32);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + S);
+  uint8_t* zero_buf = smem + (size_t)S * tile_bytes;
+  float2* red = reinterpret_cast<float2*>(zero_buf + kOnlineZeroBytes);  // [2][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 64);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
   const int64_t G = gridDim.x;
   const int64_t n_rows = blockIdx.x < p.total_rows ? (p.total_rows - 1 - blockIdx.x) / G + 1 : 0;
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
   const int32_t pv = g.pitch >> 3;
-  const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
 
+  for (int i = tid; i < kOnlineZeroBytes / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(zero_buf)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();  // the zeros are visible to the bulk-store engine
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)W);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
   pdl_trigger();
-  pdl_wait();  // inputs written, outputs read by the previous kernel: done
 
-  // Row j of this CTA -> element offset of its first column and valid count.
-  auto row_of = [&](int64_t j, int64_t& off, int32_t& valid) {
-    const int64_t flat = blockIdx.x + j * G;
-    const int64_t b = flat / g.rows;
-    const int32_t i = (int32_t)(flat - b * g.rows);
-    off = b * g.batch_stride + (int64_t)i * g.pitch;
-    valid = valid_cols(g, i);
-  };
-
-  // ---- producer state (meaningful in thread 0 only) ----
-  int64_t loads = 0;     // copies issued so far (load index of the next copy)
-  int64_t released = 0;  // copies whose stage has been handed back
-  int64_t pj = 0;        // producer cursor: row, pass, tile
-  int32_t ppass = 0, pt = 0;
-  int64_t p_off = 0;
-  int32_t p_nvec = 0, p_nt = 0;
-  bool p_res = false;
-  uint64_t pol_first = 0;
-  if (tid == 0 && n_rows > 0) {
-    int32_t valid;
-    row_of(0, p_off, valid);
-    p_nvec = (valid + 7) >> 3;
-    p_nt = (p_nvec + tile_vec - 1) / tile_vec;
-    p_res = p_nt <= S;
-    pol_first = policy_evict_first();
-  }
-  auto produce = [&]() {
-    if (skip_loads) return;
-    while (loads - released < S && pj < n_rows) {
-      const int s = (int)(loads % S);
-      const int32_t v0 = pt * tile_vec;
-      const int32_t nvt = min(tile_vec, p_nvec - v0);
-      mbar_arrive_expect_tx(&full[s], (uint32_t)nvt * 16u);
-      const uint16_t* src = g.in + p_off + (int64_t)v0 * 8;
-      if (ppass == 0)
-        bulk_g2s(tiles + (size_t)s * tile_bytes, src, (uint32_t)nvt * 16u, &full[s]);
-      else
-        bulk_g2s_hint(tiles + (size_t)s * tile_bytes, src, (uint32_t)nvt * 16u, &full[s], pol_first);
-      ++loads;
-      if (++pt == p_nt) {
-        pt = 0;
-        if (ppass == 0 && !p_res) {
-          ppass = 1;
-        } else {
-          ppass = 0;
-          if (++pj < n_rows) {
-            int32_t valid;
-            row_of(pj, p_off, valid);
-            p_nvec = (valid + 7) >> 3;
-            p_nt = (p_nvec + tile_vec - 1) / tile_vec;
-            p_res = p_nt <= S;
+  if (warp == W) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0 || skip_loads) return;
+    // The first S tiles' rows into L2 while the previous kernel in the stream
+    // finishes (a prefetch consumes no data; L2 is where every write lands).
+    {
+      int32_t n = 0;
+      for (int64_t j = 0; j < n_rows && n < S; ++j) {
+        int64_t off;
+        int32_t valid;
+        online_row(g, j, off, valid);
+        const int32_t nvec = (valid + 7) >> 3;
+        for (int32_t v0 = 0; v0 < nvec && n < S; v0 += tile_vec, ++n)
+          bulk_prefetch_l2(g.in + off + (int64_t)v0 * 8, (uint32_t)min(tile_vec, nvec - v0) * 16u);
+      }
+    }
+    pdl_wait();  // inputs written, outputs read by the previous kernel: done
+    const uint64_t pol_first = policy_evict_first();
+    bool aborted = false;
+    int64_t li = 0;  // load index of the next copy
+    for (int64_t j = 0; j < n_rows && !aborted; ++j) {
+      int64_t off;
+      int32_t valid;
+      online_row(g, j, off, valid);
+      const int32_t nvec = (valid + 7) >> 3;
+      const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
+      const bool resident = nt <= S;
+      // Masked columns and pitch padding: zeros, by bulk stores.
+      for (int32_t z = nvec; z < pv; z += kOnlineZeroBytes / 16)
+        bulk_s2g(g.out + off + (int64_t)z * 8, zero_buf, (uint32_t)min(kOnlineZeroBytes / 16, pv - z) * 16u);
+      bulk_commit();
+      bulk_wait_read_16();
+      for (int pass = 0; pass < (resident ? 1 : 2) && !aborted; ++pass) {
+        for (int32_t t = 0; t < nt; ++t, ++li) {
+          const int s = (int)(li % S);
+          if (li >= S) {
+            if (!mbar_wait_bounded(&empty[s], (uint32_t)(((li / S) - 1) & 1), g.timeout_ns)) {
+              aborted = true;
+              *abort_flag = 1;
+              if (g.status) atomicOr(g.status, kStatusTimeout);
+              break;
+            }
+            if (*abort_flag) {  // the consumers gave up
+              aborted = true;
+              break;
+            }
           }
+          const int32_t v0 = t * tile_vec;
+          const uint32_t bytes = (uint32_t)min(tile_vec, nvec - v0) * 16u;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          if (pass == 0)
+            bulk_g2s(tiles + (size_t)s * tile_bytes, g.in + off + (int64_t)v0 * 8, bytes, &full[s]);
+          else
+            bulk_g2s_hint(tiles + (size_t)s * tile_bytes, g.in + off + (int64_t)v0 * 8, bytes, &full[s],
+                          pol_first);
         }
       }
     }
-  };
-  if (tid == 0) produce();
-
-  int64_t base = 0;  // load index of the current row's first tile (same in every thread)
-  bool aborted = false;
-  for (int64_t j = 0; j < n_rows && !aborted; ++j) {
-    int64_t off;
-    int32_t valid;
-    row_of(j, off, valid);
-    const int32_t nvec = (valid + 7) >> 3;
-    const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
-    const bool resident = nt <= S;
-
-    // Pass 1: online (max, sum) over this thread's vectors.
-    float m = -INFINITY, s = 0.f;
-    bool timed_out = false;  // after one expired wait, skip the rest of the row's waits
-    for (int32_t t = 0; t < nt; ++t) {
-      const int64_t idx = base + t;
-      const int st = (int)(idx % S);
-      if (timed_out || !mbar_wait_bounded(&full[st], (uint32_t)((idx / S) & 1), g.timeout_ns)) {
-        if (!timed_out && g.status) atomicOr(g.status, kStatusTimeout);
-        timed_out = true;
-        *abort_flag = 1;
-      } else {
-#pragma unroll
-        for (int q = 0; q < VPT; ++q) {
-          const int32_t lv = tid + q * nthreads;  // vector within the tile
-          const int32_t v = t * tile_vec + lv;    // vector within the row
-          if (v < nvec) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * tile_bytes + (size_t)lv * 16);
-            const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
-            const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-            const float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
-            const int32_t lim = valid - v * 8;
-            float vm = -INFINITY;
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if (e < lim) vm = fmaxf(vm, z[e]);
-            const float mn = fmaxf(m, vm);
-            float acc = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc += e < lim ? ex2((z[e] - mn) * sl) : 0.f;
-            s = (m == -INFINITY ? 0.f : s * ex2((m - mn) * sl)) + acc;
-            m = mn;
-          }
-        }
-      }
-      if (!resident) {
-        __syncthreads();  // tile consumed by every thread
-        if (*abort_flag) { aborted = true; break; }
-        if (tid == 0) { released = idx + 1; produce(); }
-      }
-    }
-    if (aborted) break;
-
-    // Row statistics: warp butterflies of (m, s), then across warps.
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      online_merge(m, s, m2, s2, sl);
-    }
-    if (lane == 0) red[warp] = make_float2(m, s);
-    __syncthreads();
-    if (*abort_flag) { aborted = true; break; }
-    float2 w = lane < n_warps ? red[lane] : make_float2(-INFINITY, 0.f);
-    float rm = w.x, rs = w.y;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, rm, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, rs, o);
-      online_merge(rm, rs, m2, s2, sl);
-    }
-    const float inv = rcp_rn(rs);
-    __syncthreads();  // red[] is rewritten by the next row
-
-    // Pass 2: normalise and write.
-    uint16_t* out_row = g.out + off;
-    for (int32_t t = 0; t < nt; ++t) {
-      const int64_t idx = resident ? base + t : base + nt + t;
-      const int st = (int)(idx % S);
-      bool ok = true;
-      if (!resident) {
-        ok = mbar_wait_bounded(&full[st], (uint32_t)((idx / S) & 1), g.timeout_ns);
-        if (!ok) {
-          *abort_flag = 1;
-          if (g.status) atomicOr(g.status, kStatusTimeout);
-        }
-      }
-      if (ok) {
-#pragma unroll
-        for (int q = 0; q < VPT; ++q) {
-          const int32_t lv = tid + q * nthreads;
-          const int32_t v = t * tile_vec + lv;
-          if (v < nvec) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(tiles + (size_t)st * tile_bytes + (size_t)lv * 16);
-            const float2 f0 = half2_bits_to_float2(raw.x), f1 = half2_bits_to_float2(raw.y);
-            const float2 f2 = half2_bits_to_float2(raw.z), f3 = half2_bits_to_float2(raw.w);
-            float z[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
-            const int32_t lim = valid - v * 8;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) z[e] = e < lim ? ex2((z[e] - rm) * sl) * inv : 0.f;
-            uint4 o;
-            o.x = float2_to_half2_bits(z[0], z[1]);
-            o.y = float2_to_half2_bits(z[2], z[3]);
-            o.z = float2_to_half2_bits(z[4], z[5]);
-            o.w = float2_to_half2_bits(z[6], z[7]);
-            *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = o;
-          }
-        }
-      }
-      // The tile is written out: hand its stage back (this row's next tiles
-      // are already in their stages; the stage fills with a later tile).
-      __syncthreads();
-      if (*abort_flag) { aborted = true; break; }
-      if (tid == 0) { released = idx + 1; produce(); }
-    }
-    if (aborted) break;
-    base += resident ? nt : 2 * nt;
-
-    for (int32_t v = nvec + tid; v < pv; v += nthreads)
-      *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = make_uint4(0u, 0u, 0u, 0u);
+    bulk_wait_all();
+    // After an abort: let this CTA's copies in flight land (bounded).
+    if (aborted)
+      for (int64_t r = (li > S ? li - S : 0); r < li; ++r)
+        (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+    return;
   }
 
-  // After a timeout: let this CTA's copies in flight land (bounded).
-  if (tid == 0 && aborted) {
-    for (int64_t r = released; r < loads; ++r)
-      (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
-  }
+  // ------------------------------------------------------------ consumers
+  pdl_wait();  // their stores follow the previous kernel's reads
+  if (g.scale * kLog2e == 0.f)
+    online_consumers<VPT, true>(p, tiles, red, full, empty, abort_flag, n_rows, warp, lane, W);
+  else
+    online_consumers<VPT, false>(p, tiles, red, full, empty, abort_flag, n_rows, warp, lane, W);
 }
 
 }  // namespace cs

@@ -191,9 +191,11 @@ int cs_plan_set_row_split(cs_plan *plan, int32_t split_row, int32_t split_offset
 
 /* Tuning knobs (0 / -1 = automatic): vectors per thread of the TMA /
  * PIPELINE kernels (2, 4 or 8; 16 + i selects compiled variant i of the
- * row-resident kernel directly) or of the ONLINE kernel (2: 256-thread CTAs
- * with 8 KB tiles, 1: 1024-thread CTAs with 16 KB tiles, 3: each row held
- * whole in the shared memory of a cluster of 2, 4 or 8 CTAs that exchange
+ * row-resident kernel directly) or of the ONLINE kernel (0: automatic, which
+ * is 160-thread CTAs with 4 KB tiles for rows of up to 8192 columns and the
+ * shape of 2 beyond; 2: 288-thread CTAs, 8 consumer warps with 8 KB tiles;
+ * 1: 1024-thread CTAs, 31 consumer warps with 15.5 KB tiles; 3: each row held
+ * whole in the shared memory of a cluster of 2 to 16 CTAs that exchange
  * their partial statistics through distributed shared memory; 2..8 rows in
  * flight per cluster), ring stages of the TMA / PIPELINE / ONLINE
  * kernels (1..32; fewer where shared memory does not hold them), L2
