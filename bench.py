@@ -178,8 +178,11 @@ def head_range(matrices: int, parts: int, rank: int) -> tuple[int, int]:
     return a, b - a
 
 
-def rank_share(w: dict, world: int, rank: int, weak: bool, contiguous: bool):
-    """(first matrix, matrices, row segments, scaling, job matrices) of one rank."""
+def rank_share(w: dict, world: int, rank: int, weak: bool, contiguous: bool,
+               row_block: tuple[int, int] | None = None):
+    """(first matrix, matrices, row segments, scaling, job matrices) of one rank.
+    `row_block` (profiling captures of one GPU only): rows [a, a + n) of a
+    single matrix instead of the rank's shard."""
     if w["shard"] == "heads":
         if weak:
             # Every rank runs its own full batch of independent heads
@@ -187,6 +190,8 @@ def rank_share(w: dict, world: int, rank: int, weak: bool, contiguous: bool):
             return rank * w["matrices"], w["matrices"], [(0, w["rows"])], "weak", w["matrices"] * world
         first_b, n_local = head_range(w["matrices"], world, rank)
         return first_b, n_local, [(0, w["rows"])], "strong", w["matrices"]
+    if row_block is not None:
+        return 0, w["matrices"], [row_block], "strong", w["matrices"]
     segs = rank_segments(w["rows"], w["cols"], world, rank, fold=not contiguous)
     return 0, w["matrices"], segs, "strong", w["matrices"]
 
@@ -205,8 +210,9 @@ def job_config(args, w: dict, world: int) -> tuple[dict, str]:
     """The `config` object of the JSON line and the scaling label. Both arms
     (this library and --impl reference) print exactly this, computed without
     loading either implementation."""
+    row_block = getattr(args, "row_block", None)
     first_b, n_local, segs, scaling, job_matrices = rank_share(w, world, 0, args.weak,
-                                                               args.contiguous_rows)
+                                                               args.contiguous_rows, row_block)
     _, _, l2 = rotation(w, n_local, sum(n for _, n in segs))
     cfg = {"workload": w["desc"], "name": args.workload, "matrices": job_matrices,
            "matrices_per_rank": n_local, "rows": w["rows"], "cols": w["cols"], "pitch": w["pitch"],
@@ -217,6 +223,8 @@ def job_config(args, w: dict, world: int) -> tuple[dict, str]:
                      if not args.contiguous_rows and can_fold(w["rows"], w["cols"], world) else
                      "contiguous row blocks of one matrix, equal causal cost"),
            "l2": l2}
+    if row_block is not None:
+        cfg["row_block"] = {"first_row": args.row_block[0], "rows": args.row_block[1]}
     return cfg, scaling
 
 
@@ -403,7 +411,19 @@ def main() -> int:
                     help="vec,stages,l2_hint,zero_fill_tma (0/-1 = automatic)")
     ap.add_argument("--matrices", type=int, default=0,
                     help="override the number of matrices (profiling captures only)")
+    ap.add_argument("--row-block", default="",
+                    help="FIRST:COUNT rows of a single-matrix workload on one GPU "
+                         "(profiling captures only)")
     args = ap.parse_args()
+    if args.row_block:
+        a, n = (int(v) for v in args.row_block.split(":"))
+        w0 = WORKLOADS[args.workload]
+        if w0["shard"] != "rows" or args.gpus != 1 or not (0 <= a and 0 < n and a + n <= w0["rows"]):
+            raise SystemExit("--row-block: FIRST:COUNT inside a single-matrix workload, on one GPU")
+        args.row_block = (a, n)
+        args.no_e2e = args.no_cpu_baseline = True  # a kernel capture, not a bench line
+    else:
+        args.row_block = None
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
         args.warmup = 3
@@ -442,7 +462,7 @@ def main() -> int:
     # mirror, stored one after the other) or contiguous blocks. No exchange
     # between ranks on this path.
     first_b, n_local, segs, scaling, job_matrices = rank_share(w, world, rank, args.weak,
-                                                               args.contiguous_rows)
+                                                               args.contiguous_rows, args.row_block)
     config, _ = job_config(args, w, world)
     rows = sum(n for _, n in segs)
     r0 = segs[0][0]
@@ -520,6 +540,8 @@ def main() -> int:
     ms_step = float(t.item()) / args.steps
     alg_local = info["algorithmic_bytes"]
     alg_total = cs.roofline_bytes(rows_full, cols) * job_matrices
+    if args.row_block is not None:
+        alg_total = alg_local  # a block of rows only (profiling captures)
     value = alg_total / (ms_step / 1e3) / 1e9
 
     peak, peak_kind = measured_peak()
