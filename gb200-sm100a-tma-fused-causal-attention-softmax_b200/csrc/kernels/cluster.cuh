@@ -26,7 +26,7 @@
 //    slot of row j + S only after it has received every CTA's partial of row
 //    j + S - 1, which each CTA sends after reading the slot of row j.
 //
-// No load is multicast: every CTA loads its own blocks from global memory.
+// Every CTA loads its own blocks from global memory with plain bulk copies.
 // Every wait is bounded (Geometry::timeout_ns) and reports kStatusTimeout; a
 // CTA that gives up stops sending partials, so its peers' waits run out too.
 // A cluster barrier after the barriers are initialised, and one before exit,

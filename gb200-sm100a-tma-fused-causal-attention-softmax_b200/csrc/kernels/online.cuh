@@ -19,8 +19,9 @@
 //    and the exponents (x - m) * sl run on packed f32 pairs (x == m gives
 //    exactly 0 at any scale, up to 1e30); the row's pairs are merged with a
 //    redux max and a rescaled warp sum, and one consumer-only barrier per row;
-//  * pass 2 recomputes exp, scales by the reciprocal of the sum and writes
-//    16-byte vectors straight from registers. When the row fits the ring it
+//  * pass 2 writes p = 2^((x - M) * sl - log2 S), the reciprocal of the sum
+//    folded into the exponent (one packed fma), as 16-byte vectors straight
+//    from registers; a zero scale keeps 1 * RN(1/S). When the row fits the ring it
 //    stays resident in shared memory between the passes, so HBM sees a single
 //    read, and pass 2 hands each tile back as soon as it is written out, so
 //    the next row's tiles stream in while this row's go out; longer rows are
@@ -190,6 +191,9 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
     const float inv = rcp_rn(rs);
     const float2 inv2 = make_float2(inv, inv);
     const float2 nM2 = make_float2(-rm, -rm);
+    float lgs;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(lgs) : "f"(rs));
+    const float2 nl2 = make_float2(-lgs, -lgs);
 
     // Pass 2: normalise and write; each tile's stage is handed back after it.
     uint16_t* out_row = g.out + off;
@@ -217,10 +221,10 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
                 x.x = (w4[e] & 0xFFFFu) == kHalfNegInf ? 0.f : 1.f;
                 x.y = (w4[e] >> 16) == kHalfNegInf ? 0.f : 1.f;
               } else {
-                const float2 d = __fmul2_rn(__fadd2_rn(__half22float2(bits_h2(w4[e])), nM2), sl2);
+                const float2 d = __ffma2_rn(__fadd2_rn(__half22float2(bits_h2(w4[e])), nM2), sl2, nl2);
                 x = make_float2(ex2(d.x), ex2(d.y));
               }
-              const float2 pr = __fmul2_rn(x, inv2);
+              const float2 pr = kZeroScale ? __fmul2_rn(x, inv2) : x;
               o[e] = float2_to_half2_bits(pr.x, pr.y);
             }
             *reinterpret_cast<uint4*>(out_row + (int64_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
