@@ -38,7 +38,6 @@ constexpr int64_t kRingBytesPerSm = 72 * 1024;  // row-resident ring bytes per S
 constexpr int kMaxAutoStages = 8;
 constexpr int kOnlineDefaultStages = 8;
 constexpr int kMaxStages = 32;  // ring depth a tuning request may ask for (shared memory decides the rest)
-constexpr int kOnlineLongRowStages = 4;
 constexpr int64_t kI32Max = 2147483647;
 constexpr int64_t kMaxUnitsPerLaunch = int64_t(1) << 30;  // row-resident kernel, 32-bit unit index
 
@@ -533,24 +532,30 @@ int plan_online(const DeviceInfo& d, const Geometry& g, const Tuning& t, LaunchP
   auto max_stages_for = [&](int64_t tile_bytes) {
     return (int)std::min<int64_t>(kMaxStages, (d.max_smem_optin - cs::online_tail_bytes(kMaxStages)) / tile_bytes);
   };
-  const int vpt = t.vec == 1 ? 1 : 2;
-  // Automatic shape: rows of at most two default tiles take the short shape
-  // (measured on B200 at 64 x 4096^2: 3182 GB/s with six CTAs per SM against
-  // 2307 for the default shape's three); longer rows the default shape,
-  // which leads at 32768, 70000 and 100000 columns.
+  // Automatic shape, by the widest row (measured on B200, GB/s):
+  //  * at most two default tiles: the short shape, six CTAs per SM
+  //    (64 x 4096^2: 4395 against 3161 for the default shape);
+  //  * up to the default ring (8 tiles, 32768 columns): the default shape,
+  //    three CTAs per SM (32768^2 forced: 5452 against 4828 for the wide);
+  //  * longer rows: the wide shape, one CTA per SM with the deepest ring
+  //    that fits (13 stages of 15.5 KB hold rows of up to ~111K columns
+  //    resident): 65536 / 70000 / 98304 / 100000 / 131072 columns 4685 /
+  //    5043 / 5030 / 5080 / 4687 against 4432 / 4558 / 4137 / 4116 / 4002
+  //    for the default shape on 4 stages (two fetches, 4 CTAs per SM).
   const bool short_rows = t.vec == 0 && widest_vec <= 2 * (int64_t)cs::kOnlineTileVec;
+  const bool long_rows = t.vec == 0 && widest_vec > (int64_t)kOnlineDefaultStages * cs::kOnlineTileVec;
+  const int vpt = (t.vec == 1 || long_rows) ? 1 : 2;
   const int threads = vpt == 1 ? cs::kOnlineWideThreads : short_rows ? cs::kOnlineShortThreads : cs::kOnlineThreads;
   const int64_t tile_vec = cs::online_tile_vec(threads, vpt);
   int stages = t.stages;
-  if (!t.stages) {
-    // Rows that fit the default ring stay resident (one HBM read); longer
-    // rows are fetched twice, on a 4-stage ring, which lets 4 CTAs share an
-    // SM instead of 3 (measured on B200 at 2048 x 100000 columns: 3824
-    // against 3276 GB/s for 8 stages; 5 and 6 stages tie with 4).
-    const int64_t tiles = (widest_vec + tile_vec - 1) / tile_vec;
-    stages = tiles <= kOnlineDefaultStages ? kOnlineDefaultStages : kOnlineLongRowStages;
-  }
   const int64_t tile_bytes = tile_vec * 16;
+  if (!t.stages) {
+    // Rows that fit the ring stay resident (one HBM read); longer ones are
+    // fetched twice. The wide shape takes the deepest ring that fits; the
+    // others 8 stages (8 against 4 on the default shape: +3 to +7% at 65536
+    // to 100000 columns, -1% at 131072).
+    stages = vpt == 1 ? max_stages_for(tile_bytes) : kOnlineDefaultStages;
+  }
   stages = std::max(1, std::min(stages, max_stages_for(tile_bytes)));
   const int smem = (int)(stages * tile_bytes) + cs::online_tail_bytes(stages);
   void* fn = vpt == 1 ? reinterpret_cast<void*>(&cs::online_kernel<1>) : reinterpret_cast<void*>(&cs::online_kernel<2>);

@@ -70,15 +70,47 @@ __host__ __device__ constexpr int online_tail_bytes(int stages) {
   return kOnlineZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
 }
 
-// Flat row j of this CTA -> element offset of its first column and its
-// number of causal (valid) columns.
-__device__ __forceinline__ void online_row(const Geometry& g, int64_t j, int64_t& off, int32_t& valid) {
-  const int64_t flat = (int64_t)blockIdx.x + j * (int64_t)gridDim.x;
-  const int64_t b = flat / g.rows;
-  const int32_t i = (int32_t)(flat - b * g.rows);
-  off = b * g.batch_stride + (int64_t)i * g.pitch;
-  valid = valid_cols(g, i);
-}
+// This CTA's rows, flat indices blockIdx.x + j*gridDim.x, walked without a
+// division per row: (matrix, row) advances by (G / rows, G % rows) with one
+// carry. Gives each row's element offset and causal (valid) column count.
+struct OnlineRows {
+  int64_t b;       // matrix
+  int32_t i;       // row within the matrix
+  int64_t step_b;  // gridDim.x / rows
+  int32_t step_i;  // gridDim.x % rows
+  __device__ __forceinline__ explicit OnlineRows(const Geometry& g) {
+    // 32-bit: the grid and the row count are below 2^31.
+    const uint32_t rows = (uint32_t)g.rows;
+    b = blockIdx.x / rows;
+    i = (int32_t)(blockIdx.x - (uint32_t)b * rows);
+    step_b = gridDim.x / rows;
+    step_i = (int32_t)(gridDim.x - (uint32_t)step_b * rows);
+  }
+  __device__ __forceinline__ void next(const Geometry& g) {
+    b += step_b;
+    i += step_i;
+    if (i >= g.rows) {
+      i -= g.rows;
+      ++b;
+    }
+  }
+  __device__ __forceinline__ int64_t offset(const Geometry& g) const {
+    return b * g.batch_stride + (int64_t)i * g.pitch;
+  }
+};
+
+// A position in the ring: stage and the parity of its current phase,
+// advanced one tile at a time (no division by the ring depth).
+struct RingPos {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int S) {
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
 
 // The W consumer warps: both passes over every row of the CTA. A lane takes
 // vectors warp*32 + lane + q*32W (q < VPT) of each tile, so each warp reads
@@ -86,7 +118,7 @@ __device__ __forceinline__ void online_row(const Geometry& g, int64_t j, int64_t
 template <int VPT, bool kZeroScale>
 __device__ __forceinline__ void online_consumers(const OnlineParams& p, const uint8_t* tiles, float2* red,
                                                  uint64_t* full, uint64_t* empty, volatile int* abort_flag,
-                                                 int64_t n_rows, int warp, int lane, int W) {
+                                                 int warp, int lane, int W) {
   const Geometry& g = p.g;
   const int S = p.stages;
   const int32_t tile_vec = 32 * W * VPT;
@@ -94,11 +126,12 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
   const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   const float2 sl2 = make_float2(sl, sl);
   const int32_t lv0 = warp * 32 + lane;
-  int64_t idx = 0;  // load index of the current row's first tile
-  for (int64_t j = 0; j < n_rows; ++j) {
-    int64_t off;
-    int32_t valid;
-    online_row(g, j, off, valid);
+  OnlineRows rows(g);
+  RingPos first;  // ring position of the current row's first tile
+  // A flat row is inside the launch exactly when its matrix index is.
+  for (int64_t j = 0; rows.b < g.batch; ++j, rows.next(g)) {
+    const int64_t off = rows.offset(g);
+    const int32_t valid = valid_cols(g, rows.i);
     const int32_t nvec = (valid + 7) >> 3;
     const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
     const bool resident = nt <= S;
@@ -116,10 +149,10 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
     float m = -INFINITY;
     float2 acc = make_float2(0.f, 0.f);
     bool bad = false;  // a wait ran out: skip the rest of the row's waits
-    for (int32_t t = 0; t < nt; ++t) {
-      const int64_t li = idx + t;
-      const int st = (int)(li % S);
-      if (!bad && !mbar_wait_bounded(&full[st], (uint32_t)((li / S) & 1), g.timeout_ns)) {
+    RingPos pos = first;
+    for (int32_t t = 0; t < nt; ++t, pos.next(S)) {
+      const int st = pos.s;
+      if (!bad && !mbar_wait_bounded(&full[st], pos.ph, g.timeout_ns)) {
         bad = true;
         *abort_flag = 1;
         if (g.status) atomicOr(g.status, kStatusTimeout);
@@ -197,10 +230,10 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
 
     // Pass 2: normalise and write; each tile's stage is handed back after it.
     uint16_t* out_row = g.out + off;
-    for (int32_t t = 0; t < nt; ++t) {
-      const int64_t li = resident ? idx + t : idx + nt + t;
-      const int st = (int)(li % S);
-      if (!resident && !bad && !mbar_wait_bounded(&full[st], (uint32_t)((li / S) & 1), g.timeout_ns)) {
+    if (resident) pos = first;  // the row's tiles again; else its second fetch follows
+    for (int32_t t = 0; t < nt; ++t, pos.next(S)) {
+      const int st = pos.s;
+      if (!resident && !bad && !mbar_wait_bounded(&full[st], pos.ph, g.timeout_ns)) {
         bad = true;
         *abort_flag = 1;
         if (g.status) atomicOr(g.status, kStatusTimeout);
@@ -234,12 +267,12 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
       __syncwarp();
       if (lane == 0 && !bad) mbar_arrive(&empty[st]);
     }
-    idx += resident ? nt : 2 * nt;
+    first = pos;
   }
 }
 
 template <int VPT>
-__global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ OnlineParams p) {
+__global__ void __launch_bounds__(1024, 1) online_kernel(const __grid_constant__ OnlineParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Geometry& g = p.g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -254,8 +287,6 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
-  const int64_t G = gridDim.x;
-  const int64_t n_rows = blockIdx.x < p.total_rows ? (p.total_rows - 1 - blockIdx.x) / G + 1 : 0;
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
   const int32_t pv = g.pitch >> 3;
 
@@ -280,11 +311,10 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
     // finishes (a prefetch consumes no data; L2 is where every write lands).
     {
       int32_t n = 0;
-      for (int64_t j = 0; j < n_rows && n < S; ++j) {
-        int64_t off;
-        int32_t valid;
-        online_row(g, j, off, valid);
-        const int32_t nvec = (valid + 7) >> 3;
+      OnlineRows pre(g);
+      for (; pre.b < g.batch && n < S; pre.next(g)) {
+        const int64_t off = pre.offset(g);
+        const int32_t nvec = (valid_cols(g, pre.i) + 7) >> 3;
         for (int32_t v0 = 0; v0 < nvec && n < S; v0 += tile_vec, ++n)
           bulk_prefetch_l2(g.in + off + (int64_t)v0 * 8, (uint32_t)min(tile_vec, nvec - v0) * 16u);
       }
@@ -293,11 +323,11 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
     const uint64_t pol_first = policy_evict_first();
     bool aborted = false;
     int64_t li = 0;  // load index of the next copy
-    for (int64_t j = 0; j < n_rows && !aborted; ++j) {
-      int64_t off;
-      int32_t valid;
-      online_row(g, j, off, valid);
-      const int32_t nvec = (valid + 7) >> 3;
+    RingPos pos;     // its ring position
+    OnlineRows rows(g);
+    for (; rows.b < g.batch && !aborted; rows.next(g)) {
+      const int64_t off = rows.offset(g);
+      const int32_t nvec = (valid_cols(g, rows.i) + 7) >> 3;
       const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
       const bool resident = nt <= S;
       // Masked columns and pitch padding: zeros, by bulk stores.
@@ -306,10 +336,11 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
       bulk_commit();
       bulk_wait_read_16();
       for (int pass = 0; pass < (resident ? 1 : 2) && !aborted; ++pass) {
-        for (int32_t t = 0; t < nt; ++t, ++li) {
-          const int s = (int)(li % S);
+        for (int32_t t = 0; t < nt; ++t, ++li, pos.next(S)) {
+          const int s = pos.s;
           if (li >= S) {
-            if (!mbar_wait_bounded(&empty[s], (uint32_t)(((li / S) - 1) & 1), g.timeout_ns)) {
+            // The stage's previous use: the phase before the current one.
+            if (!mbar_wait_bounded(&empty[s], pos.ph ^ 1u, g.timeout_ns)) {
               aborted = true;
               *abort_flag = 1;
               if (g.status) atomicOr(g.status, kStatusTimeout);
@@ -333,18 +364,23 @@ __global__ void __launch_bounds__(1024) online_kernel(const __grid_constant__ On
     }
     bulk_wait_all();
     // After an abort: let this CTA's copies in flight land (bounded).
+    // Stage k's last use is d = (pos.s - 1 - k) mod S loads back, in the
+    // current lap for k < pos.s and in the previous one otherwise.
     if (aborted)
-      for (int64_t r = (li > S ? li - S : 0); r < li; ++r)
-        (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+      for (int k = 0; k < S; ++k) {
+        const int d = (pos.s - 1 - k + S) % S;
+        if (li - 1 - d < 0) continue;
+        (void)mbar_wait_bounded(&full[k], k < pos.s ? pos.ph : pos.ph ^ 1u, g.timeout_ns);
+      }
     return;
   }
 
   // ------------------------------------------------------------ consumers
   pdl_wait();  // their stores follow the previous kernel's reads
   if (g.scale * kLog2e == 0.f)
-    online_consumers<VPT, true>(p, tiles, red, full, empty, abort_flag, n_rows, warp, lane, W);
+    online_consumers<VPT, true>(p, tiles, red, full, empty, abort_flag, warp, lane, W);
   else
-    online_consumers<VPT, false>(p, tiles, red, full, empty, abort_flag, n_rows, warp, lane, W);
+    online_consumers<VPT, false>(p, tiles, red, full, empty, abort_flag, warp, lane, W);
 }
 
 }  // namespace cs
