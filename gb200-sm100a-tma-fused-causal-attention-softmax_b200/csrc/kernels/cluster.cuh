@@ -139,9 +139,8 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
   int32_t* held_nvec = reinterpret_cast<int32_t*>(held_off + S);  // [S] producer only
   volatile int* abort_flag = reinterpret_cast<volatile int*>(held_off + 2 * S);
 
-  const int64_t nclusters = gridDim.x / C;
-  const int64_t q = blockIdx.x / C;  // this CTA's cluster
-  const int64_t n_rows = q < p.total_rows ? (p.total_rows - 1 - q) / nclusters + 1 : 0;
+  const uint32_t nclusters = gridDim.x / (uint32_t)C;
+  const uint32_t q = blockIdx.x / (uint32_t)C;  // this CTA's cluster; its rows are q + j*nclusters
   const bool skip_loads = (g.flags & kFlagSkipLoads) != 0;
   const int32_t pv = g.pitch >> 3;
   const int32_t nblk = (pv + kClusterBlockVec - 1) / kClusterBlockVec;  // blocks per padded row
@@ -165,14 +164,6 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
   cluster_sync_all();  // every CTA's barriers exist before any peer arrives on them
   pdl_trigger();
 
-  // Row j of this cluster: flat row q + j * nclusters -> element offset and valid count.
-  auto row_of = [&](int64_t j, int64_t& off, int32_t& valid) {
-    const int64_t flat = q + j * nclusters;
-    const int64_t b = flat / g.rows;
-    const int32_t i = (int32_t)(flat - b * g.rows);
-    off = b * g.batch_stride + (int64_t)i * g.pitch;
-    valid = valid_cols(g, i);
-  };
   // This CTA's blocks of a row: local block t is row block rank + t*C; the
   // number of them, and the vectors of block t that hold causal data.
   const int32_t my_blocks = nblk > (int32_t)rank ? (nblk - 1 - (int32_t)rank) / C + 1 : 0;
@@ -198,11 +189,14 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
         bulk_commit();
       };
       bool aborted = false;
-      int64_t j = 0;
-      for (; j < n_rows; ++j) {
-        const int s = (int)(j % S);
+      int64_t j = 0;   // rows issued
+      RingPos pos;     // the stage of row j
+      RowCursor cur(g, q, nclusters);
+      for (; cur.inside(g); ++j, cur.next(g), pos.next(S)) {
+        const int s = pos.s;
         if (j >= S) {
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((j / S) - 1) & 1), g.timeout_ns)) {
+          // The stage's previous row: the phase before the current one.
+          if (!mbar_wait_bounded(&empty[s], pos.ph ^ 1u, g.timeout_ns)) {
             aborted = true;
             *abort_flag = 1;
             if (g.status) atomicOr(g.status, kStatusTimeout);
@@ -215,10 +209,8 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
           store_row(s);
           bulk_wait_read_all();  // the stage is read out before it is refilled
         }
-        int64_t off;
-        int32_t valid;
-        row_of(j, off, valid);
-        const int32_t nvec = (valid + 7) >> 3;
+        const int64_t off = cur.offset(g);
+        const int32_t nvec = (valid_cols(g, cur.i) + 7) >> 3;
         uint32_t bytes = 0;
         for (int32_t t = 0; t < my_blocks; ++t) bytes += (uint32_t)block_valid_vec(t, nvec) * 16u;
         mbar_arrive_expect_tx(&full[s], bytes);
@@ -239,21 +231,29 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
         held_nvec[s] = nvec;
       }
       if (!aborted) {
-        // Outputs of the rows still held by the other stages.
-        for (int64_t jj = j; jj < j + S; ++jj) {
-          if (jj - S < 0 || jj - S >= n_rows) continue;
-          const int s = (int)(jj % S);
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((jj / S) - 1) & 1), g.timeout_ns)) {
+        // Outputs of the rows still held: the S stages from row j on hold
+        // rows j - S .. j - 1 (those that exist), each released in the phase
+        // before its position's.
+        RingPos f = pos;
+        for (int k = 0; k < S; ++k, f.next(S)) {
+          if (j + k < S) continue;
+          if (!mbar_wait_bounded(&empty[f.s], f.ph ^ 1u, g.timeout_ns)) {
             if (g.status) atomicOr(g.status, kStatusTimeout);
             break;
           }
-          store_row(s);
+          store_row(f.s);
         }
       }
       bulk_wait_all();
+      // After an abort: the loads still in flight. Stage k's last row is
+      // d = (pos.s - 1 - k) mod S rows back, in the current lap for
+      // k < pos.s and in the previous one otherwise.
       if (aborted)
-        for (int64_t r = (j > S ? j - S : 0); r < j; ++r)
-          (void)mbar_wait_bounded(&full[r % S], (uint32_t)((r / S) & 1), g.timeout_ns);
+        for (int k = 0; k < S; ++k) {
+          const int d = (pos.s - 1 - k + S) % S;
+          if (j - 1 - d < 0) continue;
+          (void)mbar_wait_bounded(&full[k], k < pos.s ? pos.ph : pos.ph ^ 1u, g.timeout_ns);
+        }
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -262,10 +262,8 @@ __global__ void __launch_bounds__(544, 1) cluster_kernel(const __grid_constant__
     const uint32_t xbar_local = smem_addr(xbar);
     int s = 0;
     uint32_t parity = 0;
-    for (int64_t j = 0; j < n_rows; ++j) {
-      int64_t off;
-      int32_t valid;
-      row_of(j, off, valid);
+    for (RowCursor cur(g, q, nclusters); cur.inside(g); cur.next(g)) {
+      const int32_t valid = valid_cols(g, cur.i);
       const int32_t nvec = (valid + 7) >> 3;
       const bool ok = mbar_wait_bounded(&full[s], parity, g.timeout_ns);
       if (!ok) {

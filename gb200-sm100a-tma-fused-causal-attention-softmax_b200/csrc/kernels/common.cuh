@@ -183,6 +183,19 @@ __device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
   return r != 0;
 }
 
+// A position in a ring of S stages: the stage and the parity of its current
+// mbarrier phase, advanced one use at a time (no division by the depth).
+struct RingPos {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int S) {
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
 // MUFU base-2 exponential (PTX ex2.approx; subnormal results flush to zero,
 // which cannot change an FP16 probability: p <= e and e < 2^-126 rounds to 0).
 __device__ __forceinline__ float ex2(float x) {

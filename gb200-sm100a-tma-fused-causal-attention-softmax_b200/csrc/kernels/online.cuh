@@ -70,48 +70,6 @@ __host__ __device__ constexpr int online_tail_bytes(int stages) {
   return kOnlineZeroBytes + 2 * 32 * 8 + 2 * stages * 8 + 16;
 }
 
-// This CTA's rows, flat indices blockIdx.x + j*gridDim.x, walked without a
-// division per row: (matrix, row) advances by (G / rows, G % rows) with one
-// carry. Gives each row's element offset and causal (valid) column count.
-struct OnlineRows {
-  int64_t b;       // matrix
-  int32_t i;       // row within the matrix
-  int64_t step_b;  // gridDim.x / rows
-  int32_t step_i;  // gridDim.x % rows
-  __device__ __forceinline__ explicit OnlineRows(const Geometry& g) {
-    // 32-bit: the grid and the row count are below 2^31.
-    const uint32_t rows = (uint32_t)g.rows;
-    b = blockIdx.x / rows;
-    i = (int32_t)(blockIdx.x - (uint32_t)b * rows);
-    step_b = gridDim.x / rows;
-    step_i = (int32_t)(gridDim.x - (uint32_t)step_b * rows);
-  }
-  __device__ __forceinline__ void next(const Geometry& g) {
-    b += step_b;
-    i += step_i;
-    if (i >= g.rows) {
-      i -= g.rows;
-      ++b;
-    }
-  }
-  __device__ __forceinline__ int64_t offset(const Geometry& g) const {
-    return b * g.batch_stride + (int64_t)i * g.pitch;
-  }
-};
-
-// A position in the ring: stage and the parity of its current phase,
-// advanced one tile at a time (no division by the ring depth).
-struct RingPos {
-  int s = 0;
-  uint32_t ph = 0;
-  __device__ __forceinline__ void next(int S) {
-    if (++s == S) {
-      s = 0;
-      ph ^= 1u;
-    }
-  }
-};
-
 // The W consumer warps: both passes over every row of the CTA. A lane takes
 // vectors warp*32 + lane + q*32W (q < VPT) of each tile, so each warp reads
 // 512 contiguous bytes per load.
@@ -126,10 +84,10 @@ __device__ __forceinline__ void online_consumers(const OnlineParams& p, const ui
   const float sl = g.scale * kLog2e;  // exponents (x - max) * scale*log2(e)
   const float2 sl2 = make_float2(sl, sl);
   const int32_t lv0 = warp * 32 + lane;
-  OnlineRows rows(g);
+  RowCursor rows(g, blockIdx.x, gridDim.x);  // this CTA's rows: blockIdx.x + j*gridDim.x
   RingPos first;  // ring position of the current row's first tile
   // A flat row is inside the launch exactly when its matrix index is.
-  for (int64_t j = 0; rows.b < g.batch; ++j, rows.next(g)) {
+  for (int64_t j = 0; rows.inside(g); ++j, rows.next(g)) {
     const int64_t off = rows.offset(g);
     const int32_t valid = valid_cols(g, rows.i);
     const int32_t nvec = (valid + 7) >> 3;
@@ -311,8 +269,8 @@ __global__ void __launch_bounds__(1024, 1) online_kernel(const __grid_constant__
     // finishes (a prefetch consumes no data; L2 is where every write lands).
     {
       int32_t n = 0;
-      OnlineRows pre(g);
-      for (; pre.b < g.batch && n < S; pre.next(g)) {
+      RowCursor pre(g, blockIdx.x, gridDim.x);
+      for (; pre.inside(g) && n < S; pre.next(g)) {
         const int64_t off = pre.offset(g);
         const int32_t nvec = (valid_cols(g, pre.i) + 7) >> 3;
         for (int32_t v0 = 0; v0 < nvec && n < S; v0 += tile_vec, ++n)
@@ -324,8 +282,8 @@ __global__ void __launch_bounds__(1024, 1) online_kernel(const __grid_constant__
     bool aborted = false;
     int64_t li = 0;  // load index of the next copy
     RingPos pos;     // its ring position
-    OnlineRows rows(g);
-    for (; rows.b < g.batch && !aborted; rows.next(g)) {
+    RowCursor rows(g, blockIdx.x, gridDim.x);  // this CTA's rows: blockIdx.x + j*gridDim.x
+    for (; rows.inside(g) && !aborted; rows.next(g)) {
       const int64_t off = rows.offset(g);
       const int32_t nvec = (valid_cols(g, rows.i) + 7) >> 3;
       const int32_t nt = (nvec + tile_vec - 1) / tile_vec;
