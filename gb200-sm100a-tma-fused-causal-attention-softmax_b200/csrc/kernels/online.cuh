@@ -5,10 +5,12 @@
 // Replaces gpu/src/main.rs:546-727 (two dense TMA passes, 2 KB tiles, one
 // tile in flight per buffer, wait_group(0) after every store):
 //
-//  * each CTA owns whole rows (flat row index blockIdx.x + j*gridDim.x) and a
-//    ring of S shared-memory tiles; a tile is W consumer warps x 32 lanes x
-//    VPT 16-byte vectors (8 warps x 2 = 8 KB by default, 31 warps x 1 =
-//    15.5 KB for the wide shape);
+//  * each CTA owns whole rows (flat row index blockIdx.x + j*gridDim.x,
+//    walked with a division-free cursor) and a ring of S shared-memory
+//    tiles; a tile is W consumer warps x 32 lanes x
+//    VPT 16-byte vectors (4 warps x 2 = 4 KB for rows of up to two default
+//    tiles, 8 warps x 2 = 8 KB by default, 31 warps x 1 = 15.5 KB for rows
+//    longer than the default ring, on the deepest ring that fits);
 //  * one producer warp keeps the ring full with 1-D TMA bulk copies of the
 //    causal prefix only, running ahead across row boundaries, and writes the
 //    masked columns and pitch padding with bulk stores from a zero buffer;
@@ -47,7 +49,6 @@ constexpr int kOnlineConsumerWarps = 8;  // the default shape: 8 KB tiles
 constexpr int kOnlineVecPerThread = 2;
 constexpr int kOnlineThreads = 32 * (kOnlineConsumerWarps + 1);
 constexpr int kOnlineTileVec = 32 * kOnlineConsumerWarps * kOnlineVecPerThread;  // 512 vectors
-constexpr int kOnlineTileBytes = kOnlineTileVec * 16;                             // 8 KB
 constexpr int kOnlineWideThreads = 1024;  // long rows: 31 consumer warps, one vector per lane
 // Rows of at most two default tiles: 4 consumer warps (4 KB tiles), so that
 // six CTAs, each with a ring of 8 stages, share an SM.
