@@ -377,7 +377,8 @@ def run_reference(args, w: dict) -> None:
         "config": config,
         "matrices_per_s": round(per_step / step, 4),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step} whole {rows}x{cols} matrices per step (a pool of "
+                         "sample": f"{per_step} whole {rows}x{cols} "
+                                   f"{'matrix' if per_step == 1 else 'matrices'} per step (a pool of "
                                    f"{pool_n} seeded matrices, cycled), rows split over {threads} "
                                    f"threads; C restatement of reference/src/lib.rs:85-108, f32, "
                                    f"glibc expf, on the host cores of rank 0"},

@@ -2,14 +2,14 @@
 with torch (plumbing only), launch through the C ABI, and compare against the
 CPU oracle. Test infrastructure.
 
-Tolerances (the north star, checked against the FP64 oracle rounded to
-half): masked entries bit-exact 0x0000; unmasked within ULP_TOL FP16 ulp or
-ABS_TOL absolute; |row sum - 1| <= ROWSUM_TOL. A row whose exactly rounded
-FP64 result already misses ROWSUM_TOL (FP16 rounding of many small
-probabilities, e.g. uniform rows of ~70000+ columns) may miss it by that much
-(ROWSUM_FLOOR_MARGIN = 0: no worse than exact rounding); every such row is
-recorded in FLOOR_LOG and counted at the end of the test session. No case of
-the suite has needed it on a B200. The f32
+Tolerances (the acceptance bar of this library, checked against the FP64
+oracle rounded to half): masked entries bit-exact 0x0000; unmasked within
+ULP_TOL FP16 ulp or ABS_TOL absolute; |row sum - 1| <= ROWSUM_TOL. A row
+whose exactly rounded FP64 result already misses ROWSUM_TOL (FP16 rounding
+of many small probabilities, e.g. uniform rows of ~70000+ columns) may miss
+it by that much (ROWSUM_FLOOR_MARGIN = 0: no worse than exact rounding);
+every such row is recorded in FLOOR_LOG and counted at the end of the test
+session. No case of the suite has needed it on a B200. The f32
 specification (reference/src/lib.rs:85-108) is held to the same element
 bound, and the reference's own verifier (host/src/lib.rs:280-328: 0.003 +
 0.003*w per element, 0.02 per row sum, non-negative, finite, masked == 0)
@@ -74,7 +74,7 @@ def layout(x: np.ndarray):
 
 def check(got: np.ndarray, x: np.ndarray, *, cols: int, scale: float, row_offset: int = 0,
           what: str = "") -> dict:
-    """Assert the north-star acceptance against the FP64 oracle and the element
+    """Assert the acceptance bar against the FP64 oracle and the element
     bound against the f32 specification; returns the acceptance report."""
     batch, rows, pitch = layout(x)
     flat_x, flat_g = x.reshape(-1), got.reshape(-1)
