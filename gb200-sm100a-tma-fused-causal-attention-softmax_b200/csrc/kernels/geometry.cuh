@@ -60,7 +60,6 @@ __host__ __device__ __forceinline__ int32_t valid_cols(const Geometry& g, int32_
   return v < g.cols ? (int32_t)v : g.cols;
 }
 
-#ifdef __CUDACC__
 // Flat rows first, first + step, first + 2 step, ... of a launch (matrix b,
 // row i), walked without a division per row: (b, i) advances by
 // (step / rows, step % rows) with one carry. A flat row is inside the launch
@@ -71,27 +70,29 @@ struct RowCursor {
   int32_t i;       // row within the matrix
   int64_t step_b;  // step / rows
   int32_t step_i;  // step % rows
-  __device__ __forceinline__ RowCursor(const Geometry& g, uint32_t first, uint32_t step) {
+  __host__ __device__ __forceinline__ RowCursor(const Geometry& g, uint32_t first, uint32_t step) {
     const uint32_t rows = (uint32_t)g.rows;
     b = first / rows;
     i = (int32_t)(first - (uint32_t)b * rows);
     step_b = step / rows;
     step_i = (int32_t)(step - (uint32_t)step_b * rows);
   }
-  __device__ __forceinline__ bool inside(const Geometry& g) const { return b < g.batch; }
-  __device__ __forceinline__ void next(const Geometry& g) {
+  __host__ __device__ __forceinline__ bool inside(const Geometry& g) const { return b < g.batch; }
+  __host__ __device__ __forceinline__ void next(const Geometry& g) {
     b += step_b;
-    i += step_i;
-    if (i >= g.rows) {
-      i -= g.rows;
+    // i and step_i are below rows < 2^31, so their sum fits 32 unsigned bits
+    // (a signed sum would overflow once rows exceeds 2^31 - step).
+    uint32_t n = (uint32_t)i + (uint32_t)step_i;
+    if (n >= (uint32_t)g.rows) {
+      n -= (uint32_t)g.rows;
       ++b;
     }
+    i = (int32_t)n;
   }
-  __device__ __forceinline__ int64_t offset(const Geometry& g) const {
+  __host__ __device__ __forceinline__ int64_t offset(const Geometry& g) const {
     return b * g.batch_stride + (int64_t)i * g.pitch;
   }
 };
-#endif
 
 // Rows of a block of n rows starting at absolute row first whose prefix is
 // shorter than cols.

@@ -12,9 +12,15 @@ tests replay those rules and compare them with the division-based formulas
 (use r of the ring lives in stage r % S, phase parity (r // S) & 1) over many
 ring depths and use counts.
 """
+import os
 import random
+import shutil
+import subprocess
 
 import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+KERNELS = os.path.join(ROOT, "gb200-sm100a-tma-fused-causal-attention-softmax_b200", "csrc", "kernels")
 
 
 class RingPos:
@@ -93,11 +99,15 @@ class RowCursor:
         self.step_b, self.step_i = step // rows, step % rows
 
     def next(self):
+        # The kernels form i + step_i in 32 unsigned bits: both are below
+        # rows < 2^31, so the sum stays below 2^32.
         self.b += self.step_b
-        self.i += self.step_i
-        if self.i >= self.rows:
-            self.i -= self.rows
+        n = self.i + self.step_i
+        assert n < 2 ** 32
+        if n >= self.rows:
+            n -= self.rows
             self.b += 1
+        self.i = n
 
 
 def test_row_cursor_walks_the_flat_rows():
@@ -116,3 +126,37 @@ def test_row_cursor_walks_the_flat_rows():
                 assert 0 <= cur.i < rows
                 cur.next()
             assert seen == list(range(first, total, grid)), (rows, grid, batch, first)
+
+
+@pytest.fixture(scope="module")
+def cursor_check(tmp_path_factory):
+    cxx = shutil.which("g++")
+    if not cxx:
+        pytest.skip("g++ not available")
+    exe = str(tmp_path_factory.mktemp("cursor") / "cursor_check")
+    subprocess.run([cxx, "-O2", "-std=c++17", "-D__host__=", "-D__device__=",
+                    "-D__forceinline__=inline", "-I", KERNELS,
+                    os.path.join(ROOT, "tests", "cursor_check.cpp"), "-o", exe], check=True)
+
+    def run(cases):
+        text = "".join(f"{r} {b} {s}\n" for r, b, s in cases)
+        out = subprocess.run([exe], input=text, capture_output=True, text=True, check=True).stdout
+        res = [tuple(int(x) for x in line.split()) for line in out.splitlines()]
+        assert len(res) == len(cases)
+        return res
+
+    return run
+
+
+def test_row_cursor_of_the_kernels_up_to_the_largest_row_count(cursor_check):
+    # The header's own RowCursor, compiled as C++: small shapes with the step
+    # above and below the row count, and matrices of up to 2^31 - 1 rows (the
+    # largest the ABI accepts), where a signed 32-bit i + step_i would
+    # overflow within the last `step` rows of every matrix.
+    rng = random.Random(5)
+    cases = [(4096, 3, 444), (7, 5, 148), (1, 9, 888), (100, 3, 100), (32768, 2, 3552),
+             (2 ** 31 - 1, 2, 888), (2 ** 31 - 700, 2, 888), (2 ** 31 - 1, 1, 148 * 7)]
+    cases += [(rng.randint(1, 5000), rng.randint(1, 6), rng.randint(1, 3000)) for _ in range(300)]
+    for (rows, batch, step), (visits, ok) in zip(cases, cursor_check(cases)):
+        assert ok == 1, (rows, batch, step)
+        assert visits > 0
