@@ -286,13 +286,15 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
     };
     // The static sequence first, first + G, ... as (matrix, in-matrix index)
     // cursors stepped without division.
+    // kk and gr are below upm < 2^31, so their sum fits 32 unsigned bits.
     auto step = [&](int32_t& b, int32_t& kk) {
-      kk += gr;
+      uint32_t n = (uint32_t)kk + (uint32_t)gr;
       b += gq;
-      if (kk >= upm) {
-        kk -= upm;
+      if (n >= (uint32_t)upm) {
+        n -= (uint32_t)upm;
         ++b;
       }
+      kk = (int32_t)n;
     };
     // Masked columns and pitch padding of a unit: bulk stores from the zero buffer.
     auto zero_fill = [&](const UnitGeo& u) {
@@ -597,11 +599,14 @@ __global__ void __launch_bounds__(MAXT, MINB) rowres_kernel(const __grid_constan
           *reinterpret_cast<uint4*>(out_row + (int64_t)zi * 8) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    kk += gr;
-    b += gq;
-    if (kk >= upm) {
-      kk -= upm;
-      ++b;
+    {  // next static unit; kk + gr < 2 * upm < 2^32 in unsigned arithmetic
+      uint32_t n = (uint32_t)kk + (uint32_t)gr;
+      b += gq;
+      if (n >= (uint32_t)upm) {
+        n -= (uint32_t)upm;
+        ++b;
+      }
+      kk = (int32_t)n;
     }
     if (++s == S) {
       s = 0;
